@@ -272,6 +272,31 @@ def interaction_chunked(x, v, W, edge_index, n_atoms, chunk=8192, eps=1e-8):
     return out
 
 
+def interaction_hoisted(x, v, W, edge_index, n_atoms, chunk=4096, eps=1e-8):
+    """interaction() with the sums reordered for large systems (float64 checker):
+    B[n, ci, m1, m2] = sum_{e: dst=n} x[src e, ci, m1] Y_e[m2], then per path
+    out[n, co, lo] += sum_ci W[p, ci, co] sum_{m1, m2} cg[m1, m2, lo] B[n, ci, m1, m2].
+    Equal in exact arithmetic to the per-edge form of
+    benchmarks/benchmark_e2e_mace.py:323-350 (W does not depend on the edge and
+    the TP is linear in x (x) Y); tests/test_oracle_golden.py checks the two
+    agree, with gradients, to float64 rounding.  Differentiable by autograd."""
+    ci = x.shape[1]
+    E = v.shape[0]
+    B = torch.zeros(n_atoms, ci * 16, 16, dtype=x.dtype)
+    for s in range(0, E, chunk):
+        ei = edge_index[:, s:s + chunk]
+        Y = sh(unit(v[s:s + chunk], eps), 3)
+        xs = x[ei[0]].reshape(-1, ci * 16)
+        B = B.index_add(0, ei[1], xs.unsqueeze(2) * Y.unsqueeze(1))
+    B = B.reshape(n_atoms, ci, 16, 16)
+    out = torch.zeros(n_atoms, W.shape[2], 16, dtype=x.dtype)
+    for p, (l1, l2, lo, cg) in enumerate(cg_blocks(x.dtype)):
+        blk = B[:, :, l1 * l1:l1 * l1 + 2 * l1 + 1, l2 * l2:l2 * l2 + 2 * l2 + 1]
+        prod = torch.einsum("ncab,abo->nco", blk, cg)
+        out[:, :, lo * lo:lo * lo + 2 * lo + 1] += torch.einsum("nco,cd->ndo", prod, W[p])
+    return out
+
+
 # --------------------------------------------------------- neighbour list --
 
 def nl_bruteforce(positions, box, cutoff, self_loops=False):
