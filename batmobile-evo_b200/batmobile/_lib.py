@@ -27,6 +27,7 @@ _SIGNATURES = {
     "bm_set_mix_precision": (_i32, [_i32]),
     "bm_get_mix_precision": (_i32, []),
     "bm_device_error_check": (_i32, []),
+    "bm_selftest_wait_timeout": (_i32, [_p]),
     "bm_profile_start": (_i32, [_p]),
     "bm_profile_mark": (_i32, []),
     "bm_profile_stop": (_i32, []),

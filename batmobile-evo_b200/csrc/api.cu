@@ -171,17 +171,37 @@ int exclusive_scan_i32_to_i64(const int* in, int64_t* out, int64_t n, int64_t* t
 // Bounded device-side waits record a timeout here instead of hanging.
 static __device__ int g_device_error;
 static int* g_device_error_ptr[128] = {};
+static void* g_device_error_ctx[128] = {};
 static std::mutex g_flag_mu;
 static std::atomic<int> g_mix_precision{0};
+
+typedef int (*CtxGetCurrentFn)(void**);
+
+void* current_context() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(f);
+  });
+  void* ctx = nullptr;
+  if (fn && fn(&ctx) != 0) ctx = nullptr;
+  return ctx;
+}
 
 int* tc::error_flag() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return nullptr;
+  void* ctx = current_context();
   std::lock_guard<std::mutex> lk(g_flag_mu);
-  if (!g_device_error_ptr[dev]) {
+  if (!g_device_error_ptr[dev] || g_device_error_ctx[dev] != ctx) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
     g_device_error_ptr[dev] = static_cast<int*>(p);
+    g_device_error_ctx[dev] = current_context();  // the lookup above made the context current
   }
   return g_device_error_ptr[dev];
 }
@@ -354,7 +374,14 @@ int bm_device_error_check(void) {
     e = cudaMemcpy(p, &z, sizeof(int), cudaMemcpyHostToDevice);
   }
   if (e != cudaSuccess) return bm::set_error(BM_ERR_CUDA, "bm_device_error_check: %s", cudaGetErrorString(e));
-  if (v) return bm::set_error(BM_ERR_TIMEOUT, "a device-side wait timed out (tensor-core pipeline)");
+  // flag bits: 1 a bounded wait gave up, 2 an edge without its reverse in a
+  // list taken as symmetric, 4 a neighbour-list fill given fewer edges than it found
+  if (v & 1) return bm::set_error(BM_ERR_TIMEOUT, "a device-side wait timed out (pipelined kernel)");
+  if (v & 4)
+    return bm::set_error(BM_ERR_CAPACITY, "neighbor_list fill: the edge buffers hold fewer edges than the count "
+                                          "found (positions changed since the count, or a short E); extra edges "
+                                          "were dropped");
+  if (v & 2) return bm::set_error(BM_ERR_INVALID_ARG, "csr_reverse: an edge has no reverse edge (list not symmetric)");
   return BM_OK;
 }
 
@@ -395,4 +422,35 @@ extern "C" int bm_probe_fp32(float* scratch, int iters, int blocks, void* stream
   BM_REQUIRE(scratch && iters > 0 && blocks > 0, "bm_probe_fp32: bad arguments");
   bm::fp32_probe_kernel<<<blocks, 256, 0, bm::as_stream(stream)>>>(scratch, iters, 0.999f, 1e-4f);
   return bm::check_launch("bm_probe_fp32");
+}
+
+// ------------------------------------------------- bounded-wait self-test --
+// One thread waits on a shared-memory mbarrier that nothing ever arrives on,
+// through the same bounded wait every pipelined kernel of the library uses.
+// The wait gives up after about a second, records the timeout in the device
+// error flag and the kernel returns, so the context stays usable.
+namespace bm {
+__global__ void wait_timeout_selftest_kernel(int* err) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) (void)tc::mbar_wait(&bar, 0, err);
+  __syncthreads();
+}
+}  // namespace bm
+
+extern "C" int bm_selftest_wait_timeout(void* stream) {
+  int* err = bm::tc::error_flag();
+  if (!err) return bm::set_error(BM_ERR_CUDA, "bm_selftest_wait_timeout: device error flag unavailable");
+  cudaStream_t st = bm::as_stream(stream);
+  bm::wait_timeout_selftest_kernel<<<1, 32, 0, st>>>(err);
+  int rc = bm::check_launch("selftest(wait timeout)");
+  if (rc) return rc;
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess)
+    return bm::set_error(BM_ERR_CUDA, "bm_selftest_wait_timeout: %s", cudaGetErrorString(e));
+  return bm_device_error_check();
 }

@@ -20,6 +20,10 @@ int set_error(int code, const char* fmt, ...);
 // Maps a CUDA error (from the launch just made) to a bm status and adds
 // `launches` to the process-wide kernel launch counter (bm_launch_count).
 int check_launch(const char* what, int launches = 1);
+// The CUDA context current on this thread (driver handle, nullptr if none).
+// Per-device caches of symbol addresses are keyed by it, so that a device
+// reset or a new primary context makes them resolve the address again.
+void* current_context();
 
 // Runtime-indexable copies of the per-group tables of cg_l3.h (device code
 // cannot index host constexpr arrays with a runtime value).

@@ -161,7 +161,7 @@ __global__ void csr_reverse_kernel(const int64_t* __restrict__ row_ptr, const in
     if (a < row_ptr[j + 1] && col[a] == i) r = a;
   }
   rev[k] = r;
-  if (r < 0) atomicExch(err, 2);
+  if (r < 0) atomicOr(err, 2);
 }
 
 }  // namespace bm

@@ -111,6 +111,20 @@ constexpr size_t kAggSmem = (size_t)kRing * kSlotBytes + 2 * kBsBytes + 16;
 constexpr int kAggThreads = kLT + 32 * (kContrWarps + kProdWarps);
 
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kLT) : "memory"); }
+// consumer_sync that also ORs a flag over all consumer threads (bar.red.or):
+// every consumer warp leaves a pipeline together when any of them gave up.
+__device__ __forceinline__ bool consumer_sync_or(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.or.pred p, 1, %2, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "n"(kLT)
+      : "memory");
+  return r != 0;
+}
 
 // Bounded spin until *turn == want; false (and *err set) after a few seconds.
 __device__ __forceinline__ bool wait_turn(const uint32_t* turn, uint32_t want, int* err) {
@@ -123,7 +137,7 @@ __device__ __forceinline__ bool wait_turn(const uint32_t* turn, uint32_t want, i
       if (t0 == 0) {
         t0 = now;
       } else if (now - t0 > 1000000000ull) {
-        atomicExch(err, 1);
+        atomicOr(err, 1);
         return false;
       }
     }
@@ -848,12 +862,15 @@ layer_target_ws_kernel(const __grid_constant__ CUtensorMap xmap, const float* __
     const bool cev = ce < Ci;
     const int sw = (ce >> 1) & 3;  // 64-byte swizzle of channel row ce
     uint32_t bi = 0, ac = 0;
+    bool stuck = false;  // a bounded wait of this warp gave up in the edge loop (warp-uniform)
     for (int64_t n = blockIdx.x; n < N && ok; n += gridDim.x) {
       const int64_t eb = row_ptr[n], ee = row_ptr[n + 1];
       if (ee <= eb) continue;
-      if (!tc::mbar_wait(&dfull, ac & 1, err)) { ok = false; break; }
+      const bool gave_up = stuck || !tc::mbar_wait(&dfull, ac & 1, err);
       ++ac;
-      consumer_sync();  // every warp is done reading the previous atom's tile
+      // every warp is done reading the previous atom's tile; if any consumer
+      // thread gave up on a wait, all consumer warps leave here together
+      if (consumer_sync_or(gave_up)) { ok = false; break; }
       {
         const int cb = (warp >> 2) * 32 + lane;
         const bool cbv = cb < Ci;
@@ -874,12 +891,16 @@ layer_target_ws_kernel(const __grid_constant__ CUtensorMap xmap, const float* __
         d2[k >> 1][2 * (k & 1)] = make_float2(v.x, v.y);
         d2[k >> 1][2 * (k & 1) + 1] = make_float2(v.z, v.w);
       }
-      for (int64_t e0 = eb; e0 < ee && ok; e0 += kBatch, ++bi) {
+      for (int64_t e0 = eb; e0 < ee && !stuck; e0 += kBatch, ++bi) {
         const int cnt = (int)imin64(kBatch, ee - e0);
         const uint32_t buf = bi % kTBufs, par = bi & 1;
-        if (!tc::mbar_wait(&full[buf], (bi / kTBufs) & 1, err)) { ok = false; break; }
+        // warp votes: the warp stays converged and meets the others at the next consumer_sync_or
+        if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[buf], (bi / kTBufs) & 1, err))) { stuck = true; break; }
         // red[par] is free once the epilogue has finished the batch two back
-        if (bi >= 2 && !tc::mbar_wait(&red_empty[par], ((bi >> 1) - 1) & 1, err)) { ok = false; break; }
+        if (bi >= 2 && !__all_sync(0xffffffffu, tc::mbar_wait(&red_empty[par], ((bi >> 1) - 1) & 1, err))) {
+          stuck = true;
+          break;
+        }
 #pragma unroll 2
         for (int j = 0; j < cnt; ++j) {
           const int sl = buf * kBatch + j;

@@ -32,6 +32,12 @@
 #include "bm_common.cuh"
 
 namespace bm {
+namespace tc {
+int* error_flag();  // device error flag of the current device (api.cu)
+}
+}  // namespace bm
+
+namespace bm {
 
 struct NLGeom {
   float L[3];
@@ -234,7 +240,7 @@ __global__ void __launch_bounds__(128) nl_pairs_kernel(int64_t N, NLGeom g, bool
                                                        const int* __restrict__ sorted_idx,
                                                        const float4* __restrict__ sorted_pos,
                                                        int* __restrict__ cnt, const int64_t* __restrict__ row_ptr,
-                                                       IdxT* __restrict__ tmp_j) {
+                                                       IdxT* __restrict__ tmp_j, int64_t E, int* __restrict__ err) {
   const int lane = threadIdx.x & 31;
   const int64_t k = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (k >= N) return;
@@ -256,7 +262,11 @@ __global__ void __launch_bounds__(128) nl_pairs_kernel(int64_t N, NLGeom g, bool
         hit = (j != i || self_loops) && pair_within(pi, sorted_pos[q], g);
       }
       const unsigned m = __ballot_sync(0xffffffffu, hit);
-      if (kWrite && hit) tmp_j[w + __popc(m & ((1u << lane) - 1u))] = (IdxT)j;
+      if (kWrite && hit) {
+        const int64_t o = w + __popc(m & ((1u << lane) - 1u));
+        if (o < E) tmp_j[o] = (IdxT)j;
+        else atomicOr(err, 4);  // buffers shorter than the counted list: drop, flag
+      }
       w += __popc(m);
       count += __popc(m);
     }
@@ -274,13 +284,13 @@ template <class IdxT>
 __global__ void __launch_bounds__(256) nl_finish_kernel(int64_t N, NLGeom g, const float* __restrict__ pos,
                                                         const int64_t* __restrict__ row_ptr,
                                                         IdxT* __restrict__ ei_src, IdxT* __restrict__ ei_dst,
-                                                        float* __restrict__ vec) {
+                                                        float* __restrict__ vec, int64_t E) {
   __shared__ IdxT stage[8][kNLStage];
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t i = (int64_t)blockIdx.x * 8 + w;
   if (i >= N) return;
   const int64_t b = row_ptr[i], d = row_ptr[i + 1] - b;
-  if (d == 0) return;
+  if (d == 0 || b + d > E) return;  // rows past a short E were dropped (flagged by the write pass)
   IdxT* row = ei_dst + b;
   if (d <= kNLStage) {
     for (int64_t k = lane; k < d; k += 32) stage[w][k] = row[k];
@@ -402,7 +412,8 @@ static int nl_count_impl(const float* pos, int64_t N, int64_t n_rows, NLGeom& g,
   if (!ws || ws_bytes < w.bytes) return set_error(BM_ERR_WORKSPACE, "neighbor_list: workspace too small");
   if ((rc = nl_prepare(pos, N, g, w, st))) return rc;
   nl_pairs_kernel<false, int64_t><<<grid_for(N * 32, 128), 128, 0, st>>>(N, g, self_loops, w.cell_of, w.cell_start,
-                                                             w.sorted_idx, w.sorted_pos, w.cnt, nullptr, nullptr);
+                                                             w.sorted_idx, w.sorted_pos, w.cnt, nullptr, nullptr,
+                                                             0, nullptr);
   if ((rc = check_launch("neighbor_list(count)"))) return rc;
   return exclusive_scan_i32_to_i64(w.cnt, row_ptr, N, w.scan_tmp, st);
 }
@@ -426,13 +437,15 @@ namespace bm {
 // cell arrays still valid in the workspace).  E = row_ptr[N].
 template <class IdxT>
 static int nl_fill_impl(const float* pos, int64_t N, const NLGeom& g, bool self_loops, const int64_t* row_ptr,
-                        IdxT* ei_src, IdxT* ei_dst, float* vec, const NLWork& w, cudaStream_t st) {
+                        IdxT* ei_src, IdxT* ei_dst, float* vec, int64_t E, const NLWork& w, cudaStream_t st) {
+  int* err = tc::error_flag();
+  if (!err) return set_error(BM_ERR_CUDA, "neighbor_list: device error flag unavailable");
   nl_pairs_kernel<true, IdxT><<<grid_for(N * 32, 128), 128, 0, st>>>(N, g, self_loops, w.cell_of, w.cell_start,
                                                                   w.sorted_idx, w.sorted_pos, nullptr, row_ptr,
-                                                                  ei_dst);
+                                                                  ei_dst, E, err);
   int rc = check_launch("neighbor_list(write)");
   if (rc) return rc;
-  nl_finish_kernel<IdxT><<<grid_for(N, 8), 256, 0, st>>>(N, g, pos, row_ptr, ei_src, ei_dst, vec);
+  nl_finish_kernel<IdxT><<<grid_for(N, 8), 256, 0, st>>>(N, g, pos, row_ptr, ei_src, ei_dst, vec, E);
   return check_launch("neighbor_list(sort)");
 }
 
@@ -457,7 +470,7 @@ static int nl_fill_rows_impl(const float* pos, int64_t N, int64_t n_rows, NLGeom
   BM_REQUIRE(E >= 0, "neighbor_list: negative edge count");
   cudaStream_t st = as_stream(stream);
   if (E == 0) return BM_OK;
-  return nl_fill_impl<int64_t>(pos, N, g, self_loops, row_ptr, edge_index, edge_index + E, vec, w, st);
+  return nl_fill_impl<int64_t>(pos, N, g, self_loops, row_ptr, edge_index, edge_index + E, vec, E, w, st);
 }
 
 }  // namespace bm
@@ -533,7 +546,7 @@ int neighbor_list_cuda(const float* positions, const float* cell, int64_t N, flo
       cudaFree(ei);
       rc = set_error(BM_ERR_CUDA, "neighbor_list_cuda: %s", cudaGetErrorString(ce));
     } else {
-      rc = nl_fill_impl<int>(positions, N, g, self_loops, row_ptr, ei, ei + E, vec, w, st);
+      rc = nl_fill_impl<int>(positions, N, g, self_loops, row_ptr, ei, ei + E, vec, E, w, st);
       if (!rc) {
         ce = cudaStreamSynchronize(st);
         if (ce != cudaSuccess) rc = set_error(BM_ERR_CUDA, "neighbor_list_cuda: %s", cudaGetErrorString(ce));

@@ -68,7 +68,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
       if (t0 == 0) {
         t0 = now;
       } else if (now - t0 > 1000000000ull) {
-        if (err) atomicExch(err, 1);
+        if (err) atomicOr(err, 1);
         return false;
       }
     }

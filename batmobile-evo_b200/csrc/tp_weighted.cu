@@ -329,7 +329,9 @@ int bm_tp_bwd(const float* x, const float* Y, const float* W, const float* G, fl
 //
 // Set-up: the first call on each device looks up the array's device address
 // with cudaGetSymbolAddress while that device is current; make that first call
-// before any stream capture.
+// before any stream capture.  The address is cached per device together with
+// the CUDA context it belongs to, and looked up again when the context changes
+// (after cudaDeviceReset, for instance).
 // ---------------------------------------------------------------------------
 #include <mutex>
 
@@ -340,19 +342,22 @@ static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
 
 static std::mutex g_noalloc_mu;
 static float* g_noalloc_ptr[128] = {};
+static void* g_noalloc_ctx[128] = {};
 
 static int noalloc_scratch(float** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return set_error(BM_ERR_CUDA, "tensor_product_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= 128) return set_error(BM_ERR_UNSUPPORTED, "tensor_product_noalloc: device %d", dev);
+  void* ctx = current_context();
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
+  if (!g_noalloc_ptr[dev] || g_noalloc_ctx[dev] != ctx) {  // first call, or a new context after a reset
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || !p)
       return set_error(BM_ERR_CUDA, "tensor_product_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
     g_noalloc_ptr[dev] = static_cast<float*>(p);
+    g_noalloc_ctx[dev] = current_context();
   }
   *out = g_noalloc_ptr[dev];
   return BM_OK;

@@ -1,5 +1,5 @@
 #!/usr/bin/env python3
-"""Benchmark of the fused SH -> TP -> scatter interaction layer.
+"""Benchmark of the fused SH -> TP -> scatter interaction layer at 5000 atoms.
 
 One step = neighbour list (PBC cell list) -> target/source CSR -> fused layer
 forward -> backward (grads w.r.t. node features, weights and, through the edge
@@ -19,8 +19,8 @@ host CPU cores (normalise -> SH -> gather -> weighted TP -> index_add, torch
 fp32, all threads, forward + autograd backward; benchmarks/benchmark_e2e_mace.py:323-350)
 over a bounded sample of the target atoms, and reports the same metric.
 
-With --gpus N > 1 (torchrun, one rank per GPU) the workload is BASELINE
-config 5: N=1,000,000 atoms in a periodic cube of side 259 A, rc 5 A (~30M
+With --gpus N > 1 (torchrun, one rank per GPU) the workload is the sharded
+1M-atom system: N=1,000,000 atoms in a periodic cube of side 259 A, rc 5 A (~30M
 edges), C=64, split into N slabs along x; every step each rank exchanges ghost
 positions and features with its two neighbours over NCCL, runs the neighbour
 list over its owned atoms' rows and the fused layer forward + backward, returns
@@ -31,6 +31,7 @@ upstream gradient of the owned atoms are drawn on each rank's GPU (seed 4+rank).
 The timed region is bracketed by a barrier; the max over ranks is reported.
 """
 import argparse
+import datetime
 import json
 import math
 import os
@@ -305,6 +306,45 @@ def measured_peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
 
 
+def layer_work(E, n_targets, n_sources, c):
+    """Algorithmic work per launch (FLOP, bounding unit) of the layer's kernels:
+    256*C FMA per edge for the edge sums (outer products or dY), 611*C per atom
+    for the CG contraction, 156*C*C per atom for each channel mix."""
+    return {
+        "layer_bwd(target)": (2.0 * 256 * c * E + 2.0 * 611 * c * n_targets, "fp32"),
+        "layer_fwd(aggregate)": (2.0 * 256 * c * E + 2.0 * 611 * c * n_targets, "fp32"),
+        "layer_bwd(source aggregate)": (2.0 * 256 * c * E + 2.0 * 611 * c * n_sources, "fp32"),
+        "tc_gemm(mix->irreps)": (2.0 * 156 * c * c * (n_targets + n_sources) / 2.0, "tensor"),
+        "tc_gemm(grad->slots)": (2.0 * 156 * c * c * n_targets, "tensor"),
+        "tc_gemm(weight grad)": (2.0 * 156 * c * c * n_targets, "tensor"),
+    }
+
+
+def roofline_of(kernels, work, fp32_peak, tf32_peak, peak_kind, peaks, traffic=None):
+    """The dominant kernel's achieved FLOP/s against its unit's measured peak."""
+    top = next((k for k in kernels if k["name"] in work), kernels[0])
+    flop, bound = work.get(top["name"], (0.0, "fp32"))
+    achieved = flop / (top["ms_per_launch"] * 1e-3) / 1e12
+    peak = fp32_peak if bound == "fp32" else tf32_peak
+    return {
+        "bound": bound, "unit": "TFLOP/s", "achieved": achieved, "peak": peak, "frac": achieved / peak,
+        "traffic": (traffic or {}).get(top["name"]),
+        "kernel": top["name"], "ms_per_launch": top["ms_per_launch"],
+        "work": "%.3f GFLOP per launch (algorithmic)" % (flop / 1e9),
+        "peak_source": ("fp32 FMA probe (bm_probe_fp32) measured in this run; MEASURED_PEAKS.json has no SIMT "
+                        "figure" if bound == "fp32" else
+                        "dense tf32 = MEASURED_PEAKS.json (%s) bf16 %.0f TF/s / 2" % (peak_kind,
+                                                                                  peaks.get("bf16_tflops", 0))),
+    }
+
+
+def kernel_table(nprof):
+    from batmobile._lib import profile_report
+    return sorted(({"name": nm, "launches_per_step": cnt / nprof, "ms_per_step": ms / nprof,
+                    "ms_per_launch": ms / cnt} for nm, cnt, ms in profile_report()),
+                  key=lambda k: -k["ms_per_step"])
+
+
 # ---------------------------------------------------------- CPU baseline --
 
 def cpu_reference_step(x, v, W, ei, n, Gs, sample_atoms):
@@ -353,9 +393,10 @@ def dist_setup():
         os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout to the one JSON line
         if torch.cuda.is_available():
             torch.cuda.set_device(local)
-            dist.init_process_group(backend="nccl", device_id=torch.device("cuda", local))
+            dist.init_process_group(backend="nccl", device_id=torch.device("cuda", local),
+                                    timeout=datetime.timedelta(seconds=300))
         else:
-            dist.init_process_group(backend="gloo")
+            dist.init_process_group(backend="gloo", timeout=datetime.timedelta(seconds=300))
     elif torch.cuda.is_available():
         torch.cuda.set_device(0)
     return world, rank, local
@@ -392,7 +433,7 @@ def run_reference(args, world, rank):
     info["value"] = val
     line = {"impl": "reference", "metric": METRIC, "value": val, "unit": "Medges/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": WORKLOAD + " (CPU: bounded sample of target atoms)", "edges": int(ei.shape[1])},
             "cpu_baseline": info,
             "e2e": {"value": val, "unit": "Medges/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -417,7 +458,7 @@ def timed_ops(ops, steps, warmup, flush):
 
 
 def run_ops_config(args, config):
-    """Secondary workloads of BASELINE.json (single GPU, not the headline line):
+    """Secondary single-GPU workloads (not the headline line):
     config 2 = spherical_harmonics + tensor_product_simple forward and backward on
     1M edges (HBM-bound: algorithmic bytes per op against the measured copy
     bandwidth); config 3 = weighted tensor_product forward + backward, N=1000,
@@ -485,9 +526,33 @@ def run_ops_config(args, config):
     print(json.dumps(line), flush=True)
 
 
+class ProfiledCompute:
+    """GpuCompute with a launch-profiler boundary before every library call, so
+    that each kernel's device time starts after the torch / NCCL work before it."""
+
+    def __init__(self, inner, lib):
+        self.inner, self.lib = inner, lib
+
+    def neighbors(self, *a):
+        self.lib.bm_profile_mark()
+        return self.inner.neighbors(*a)
+
+    def layer(self, x_l, vec, W, src, dst, graph, G_l, mark=lambda name: None):
+        def mk(name):
+            mark(name)
+            self.lib.bm_profile_mark()
+        self.lib.bm_profile_mark()
+        return self.inner.layer(x_l, vec, W, src, dst, graph, G_l, mk)
+
+    def pos_grad(self, *a):
+        self.lib.bm_profile_mark()
+        return self.inner.pos_grad(*a)
+
+
 def run_sharded(args, world, rank, local):
-    """BASELINE config 5 over `world` GPUs: slab decomposition with NCCL halo."""
-    from batmobile.distributed import SlabDecomposition, GpuCompute
+    """The 1M-atom periodic system over `world` GPUs: slab decomposition with NCCL halo."""
+    import ctypes
+    from batmobile.distributed import SlabDecomposition, GpuCompute, StageEvents
     from batmobile._lib import lib
     cfg = CFG5
     dev = torch.device("cuda", local)
@@ -511,14 +576,13 @@ def run_sharded(args, world, rank, local):
     times, edges = [], 0
     barrier(world)
     torch.cuda.synchronize()
-    if True:
-        for _ in range(args.steps):
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record()
-            _, _, _, _, edges = sd.step(comp, pos_d, x, W, G)
-            e.record()
-            e.synchronize()
-            times.append(s.elapsed_time(e))
+    for _ in range(args.steps):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        _, _, _, _, edges = sd.step(comp, pos_d, x, W, G)
+        e.record()
+        e.synchronize()
+        times.append(s.elapsed_time(e))
     clk.__exit__(None, None, None)
     barrier(world)
     launches = lib.bm_launch_count() - launches0
@@ -529,11 +593,38 @@ def run_sharded(args, world, rank, local):
         dist.all_reduce(e_all)
     E = int(e_all.item())
     value = E / (t * 1e-3) / 1e6
-    # end to end: owned positions and features in from pinned host memory,
-    # forces and the weight gradient out, every step
+
+    # per-stage device time (CUDA events between the stages, this rank; mean of 3 steps)
+    stage_ms = {}
+    for _ in range(3):
+        ev = StageEvents()
+        sd.step(comp, pos_d, x, W, G, stages=ev)
+        for k, v in ev.ms().items():
+            stage_ms[k] = stage_ms.get(k, 0.0) + v / 3
+    # per-kernel device time (launch profiler, one step) and the dominant kernel's roofline
+    lib.bm_profile_start(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    _, _, _, _, e_local = sd.step(ProfiledCompute(comp, lib), pos_d, x, W, G)
+    torch.cuda.synchronize()
+    lib.bm_profile_stop()
+    kernels = kernel_table(1)
+    n_own = own.numel()
+    n_local = n_own + sd.last_halo.n_from_left + sd.last_halo.n_from_right
+    fp32_peak = probe_fp32_tflops(lib)
+    peaks, peak_kind = measured_peaks()
+    roofline = roofline_of(kernels, layer_work(e_local, n_own, n_local, cfg["c"]), fp32_peak,
+                           peaks.get("bf16_tflops", 1590.0) / 2.0, peak_kind, peaks)
+    roofline["stage_ms_rank0"] = stage_ms
+    roofline["limiting_stage"] = max(stage_ms, key=stage_ms.get) if stage_ms else None
+    roofline["note"] = ("dominant kernel on rank 0 (library launch profiler, one step); stage_ms_rank0 = CUDA "
+                        "events between the stages of the step on rank 0")
+
+    # end to end: owned positions and features in from pinned host memory; the
+    # layer output, feature gradients, forces and the weight gradient out, every step
     pos_p, x_p = pos_h.pin_memory(), x.cpu().pin_memory()
-    gpos_p = torch.empty(own.numel(), 3).pin_memory()
+    gpos_p = torch.empty(n_own, 3).pin_memory()
     gw_p = torch.empty(34, cfg["c"], cfg["c"]).pin_memory()
+    out_p = torch.empty(n_own, cfg["c"], 16).pin_memory()
+    gx_p = torch.empty(n_own, cfg["c"], 16).pin_memory()
     e2e = []
     barrier(world)
     for i in range(max(2, args.steps // 2) + 1):
@@ -541,9 +632,11 @@ def run_sharded(args, world, rank, local):
         s.record()
         pd = pos_p.to(dev, non_blocking=True)
         xd = x_p.to(dev, non_blocking=True)
-        _, _, gw, gp, _ = sd.step(comp, pd, xd, W, G)
+        out_d, gx_d, gw, gp, _ = sd.step(comp, pd, xd, W, G)
         gpos_p.copy_(gp, non_blocking=True)
         gw_p.copy_(gw, non_blocking=True)
+        out_p.copy_(out_d, non_blocking=True)
+        gx_p.copy_(gx_d, non_blocking=True)
         e.record()
         e.synchronize()
         if i > 0:
@@ -563,10 +656,12 @@ def run_sharded(args, world, rank, local):
                 "clocks": clk.summary(),
                 "e2e": {"value": E / (t_e2e * 1e-3) / 1e6, "unit": "Medges/s", "ms_per_step": t_e2e,
                         "h2d_bytes_per_step": (pos_p.numel() + x_p.numel()) * 4,
-                        "d2h_bytes_per_step": (gpos_p.numel() + gw_p.numel()) * 4,
-                        "what": "rank 0's pinned owned positions + features in, forces + weight grads out"},
+                        "d2h_bytes_per_step": (gpos_p.numel() + gw_p.numel() + out_p.numel() + gx_p.numel()) * 4,
+                        "what": "rank 0's pinned owned positions + features in; layer output, feature gradients, "
+                                "forces and weight gradients out"},
                 "gpu_launches": launches, "gpu_launches_per_step": launches / args.steps,
-                "roofline": None, "cpu_baseline": None}
+                "roofline": roofline, "kernels": kernels,
+                "cpu_baseline": None}
         print(json.dumps(line), flush=True)
 
 
@@ -653,8 +748,10 @@ def main():
     pos_p, x_p = pin(pos_h), pin(x_h)
     gpos_p = torch.empty(CFG["n"], 3).pin_memory()
     gw_p = torch.empty_like(W_h).pin_memory()
+    out_p = torch.empty(CFG["n"], CFG["c"], 16).pin_memory()
+    gx_p = torch.empty_like(x_h).pin_memory()
     h2d = pos_p.numel() * 4 + x_p.numel() * 4
-    d2h = gpos_p.numel() * 4 + gw_p.numel() * 4
+    d2h = (gpos_p.numel() + gw_p.numel() + out_p.numel() + gx_p.numel()) * 4
     e2e_ms = []
     copy_stream = torch.cuda.Stream(device=dev)
     main = torch.cuda.current_stream()
@@ -671,9 +768,11 @@ def main():
         with torch.cuda.stream(copy_stream):
             x.copy_(x_p, non_blocking=True)
             x_ready.record()
-        _, _, gw_d, gpos_d, _ = step(x_ready=x_ready)
+        out_d, gx_d, gw_d, gpos_d, _ = step(x_ready=x_ready)
         gpos_p.copy_(gpos_d, non_blocking=True)
         gw_p.copy_(gw_d, non_blocking=True)
+        out_p.copy_(out_d, non_blocking=True)
+        gx_p.copy_(gx_d, non_blocking=True)
         e.record()
         e.synchronize()
         if i >= args.warmup:
@@ -691,57 +790,35 @@ def main():
         lib.bm_profile_mark()
         gpu_step(bm, _bm, pos, x, W, G, CFG, lib=lib)
     lib.bm_profile_stop()
-    kernels = sorted(({"name": nm, "launches_per_step": cnt / nprof, "ms_per_step": ms / nprof,
-                       "ms_per_launch": ms / cnt} for nm, cnt, ms in profile_report()),
-                     key=lambda k: -k["ms_per_step"])
+    kernels = kernel_table(nprof)
     n, c = CFG["n"], CFG["c"]
     fp32_peak = probe_fp32_tflops(lib)
     peaks, peak_kind = measured_peaks()
     tf32_peak = peaks.get("bf16_tflops", 1590.0) / 2.0   # dense tf32 = half the bf16 rate
-    # algorithmic work per launch (FLOP) and the unit bounding it, by launch site
-    agg = 2.0 * 256 * c * E + 2.0 * 611 * c * n   # edge outer products + per-atom CG
-    work = {
-        "layer_bwd(target)": (2.0 * 256 * c * E + 2.0 * 611 * c * n, "fp32"),
-        "layer_fwd(aggregate)": (agg, "fp32"),
-        "layer_bwd(source aggregate)": (agg, "fp32"),
-        "tc_gemm(mix->irreps)": (2.0 * 156 * c * c * n, "tensor"),
-        "tc_gemm(grad->slots)": (2.0 * 156 * c * c * n, "tensor"),
-        "tc_gemm(weight grad)": (2.0 * 156 * c * c * n, "tensor"),
-    }
-    # DRAM bytes (read + write) per launch at config 4 from one ncu capture of each kernel
-    # (ncu --set full --clock-control none, one launch, on this build's bench command)
+    # DRAM bytes (read + write) per launch from one ncu capture of each kernel at
+    # this workload (profiles/layer_kernels_config4_ncu_full.md gives the command)
     ncu_traffic = {
         "layer_bwd(target)": 229.65e6 + 5.04e6,
         "layer_fwd(aggregate)": 31.27e6 + 150.14e6,
         "tc_gemm(mix->irreps)": 213.12e6 + 20.42e6,
     }
-    top = next((k for k in kernels if k["name"] in work), kernels[0])
-    flop, bound = work.get(top["name"], (0.0, "fp32"))
-    achieved = flop / (top["ms_per_launch"] * 1e-3) / 1e12
-    peak = fp32_peak if bound == "fp32" else tf32_peak
+    roofline = roofline_of(kernels, layer_work(E, n, n, c), fp32_peak, tf32_peak, peak_kind, peaks, ncu_traffic)
+    roofline["traffic_unit"] = ("DRAM bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum of the "
+                                "capture in profiles/, same workload)")
     stage_ms = {k: v / 3 for k, v in stages.ms.items()}
-    roofline = {
-        "bound": bound, "unit": "TFLOP/s", "achieved": achieved, "peak": peak, "frac": achieved / peak,
-        "traffic": ncu_traffic.get(top["name"]),
-        "traffic_unit": "DRAM bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum, config 4)",
-        "kernel": top["name"], "ms_per_launch": top["ms_per_launch"],
-        "work": "%.3f GFLOP per launch (algorithmic)" % (flop / 1e9),
-        "peak_source": ("fp32 FMA probe (bm_probe_fp32) measured in this run; MEASURED_PEAKS.json has no SIMT "
-                        "figure" if bound == "fp32" else
-                        "dense tf32 = MEASURED_PEAKS.json (%s) bf16 %.0f TF/s / 2" % (peak_kind,
-                                                                                  peaks.get("bf16_tflops", 0))),
+    roofline.update({
         "layer_fraction": {
             "achieved_tflops": 3 * (2.0 * 611 * c * E + 2.0 * 156 * c * c * n) /
                                ((stage_ms["layer_fwd"] + stage_ms["layer_bwd"]) * 1e-3) / 1e12,
             "note": "reference-order algorithmic work of the whole layer (3 x CG at edge granularity + 3 x mix) "
                     "over forward + backward time"},
         "stage_ms": stage_ms,
-    }
+    })
 
     mace = mace_step_timing(bm, dev, pos, max(3, args.steps // 10), args.warmup) if world == 1 else None
 
-    # ---- the same step with the channel mix in single-pass TF32 (the north star's 2e-3
-    # tf32 gate for the mix); the headline above is the fp32-accurate 3xTF32 mix
+    # ---- the same step with the channel mix in single-pass TF32 (inside the 2e-3
+    # tolerance allowed for a tf32 mix); the headline above is the fp32-accurate 3xTF32 mix
     lib.bm_set_mix_precision(1)
     try:
         step_tf32 = GraphedStep(bm, _bm, lib, CFG, pos, x, W, G)
@@ -768,10 +845,17 @@ def main():
         from oracle import ref_ops  # noqa: F401  (CPU baseline leg only)
         ei, vec = _bm.neighbor_list(pos, [CFG["box"]] * 3, CFG["rc"])
         cpu = cpu_baseline(x_h, vec.cpu(), W_h, ei.cpu(), G_h, n)
+    ref_cuda_row = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        # comparison arm: the reference's own CUDA kernels, compiled for sm_100a
+        # from its sources (oracle/ref_cuda.py), on the same inputs
+        from oracle import ref_cuda
+        ei, vec = _bm.neighbor_list(pos, [CFG["box"]] * 3, CFG["rc"])
+        ref_cuda_row = ref_cuda.time_pipelines(x, vec, W, G, ei, n)
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "Medges/s", "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": t_step, "higher_is_better": True, "scaling": "weak",
+                "warmup": args.warmup, "ms_per_step": t_step, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic",
                 "config": {"workload": WORKLOAD, "n_atoms": n, "edges": E, "channels": c,
                            "parallelism": "replicas" if world > 1 else "single",
@@ -781,11 +865,13 @@ def main():
                         "d2h_bytes_per_step": d2h,
                         "ms_per_step_median": statistics.median(e2e_ms),
                         "ms_per_step_min_max": [min(e2e_ms), max(e2e_ms)],
-                        "what": "pinned host positions + node features in (features on a copy stream, overlapping the neighbour list), forces + weight grads out"},
+                        "what": "pinned host positions + node features in (features on a copy stream, overlapping "
+                                "the neighbour list); layer output, feature gradients, forces and weight gradients "
+                                "out"},
                 "gpu_launches": launches // args.steps * args.steps,
                 "gpu_launches_per_step": launches / args.steps,
                 "roofline": roofline, "kernels": kernels, "mace_step": mace, "tf32_mix": tf32_mix,
-                "cpu_baseline": cpu}
+                "cpu_baseline": cpu, "reference_cuda_b200": ref_cuda_row}
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist

@@ -58,7 +58,7 @@ int64_t bm_launch_count(void);
 int bm_probe_fp32(float* scratch, int iters, int blocks, void* stream);
 /* Precision of the per-path channel mixes, which run on the tensor cores:
  * 0 (default) = fp32-accurate (TF32 hi/lo split, three passes, ~1e-6 relative);
- * 1 = single-pass TF32 (~5e-4 relative; the north star's 2e-3 tf32 gate). */
+ * 1 = single-pass TF32 (~5e-4 relative; inside the 2e-3 tolerance allowed for a tf32 mix). */
 int bm_set_mix_precision(int mode);
 int bm_get_mix_precision(void);
 /* Launch profiler.  Between start and stop the library records a CUDA event on
@@ -73,8 +73,17 @@ int bm_profile_stop(void);
 int bm_profile_count(void);
 int bm_profile_entry(int i, char* name, int name_len, int64_t* launches, double* total_ms);
 /* Blocks until the current device is idle, reads and clears the device-side
- * error flag; BM_ERR_TIMEOUT if a bounded wait in a tensor-core kernel gave up. */
+ * error flag: BM_ERR_TIMEOUT if a bounded wait in a pipelined kernel gave up,
+ * BM_ERR_CAPACITY if a neighbour-list fill was given fewer edge slots than the
+ * list has (the extra edges are dropped, nothing is written past E),
+ * BM_ERR_INVALID_ARG if bm_csr_reverse met an edge without its reverse. */
 int bm_device_error_check(void);
+/* Self-test of the bounded device waits (no counterpart in the reference, which
+ * has no bounded waits): one thread waits on an mbarrier that nothing arrives
+ * on; the wait gives up after about a second and the kernel returns.  Blocks
+ * until done and returns bm_device_error_check(): BM_ERR_TIMEOUT, with the
+ * flag cleared and the context usable for the next call. */
+int bm_selftest_wait_timeout(void* stream);
 
 /* ---------------------------------------------------------------- paths -- */
 /* Replaces batteries::get_num_paths_l3 (src/tensor_product/tensor_product.cu:203). */
@@ -171,7 +180,7 @@ int bm_fused_mp_weighted(const float* x, const float* v, const float* W2, const 
                          int C_in, int C_out, void* workspace, size_t workspace_bytes,
                          void* stream);
 
-/* --------------------------------------- fused interaction layer (north star) -- */
+/* --------------------------------------- fused interaction layer --------------- */
 /* out[n,co,:] = sum over edges e with dst[e]==n of
  *     sum_p sum_ci W[p,ci,co] * CG_p(x[src[e],ci,:], Y(v[e]/max(|v[e]|,1e-8)))
  * i.e. the reference's unfused chain  normalise -> spherical_harmonics ->
@@ -254,7 +263,9 @@ int bm_edge_grad_to_pos(const float* grad_v, const int64_t* row_ptr_dst, const i
  * lengths.  Two calls: bm_nl_count fills row_ptr[N+1] (by source i); the
  * caller reads row_ptr[N] (= E), allocates edge_index[2,E] and vec[E,3], then
  * bm_nl_fill writes the edges.  Both calls must get the same positions and the
- * same workspace (the cell arrays built by the count are reused). */
+ * same workspace (the cell arrays built by the count are reused).  The fill
+ * writes at most E edges: if the count it reads holds more, the extra edges
+ * are dropped and bm_device_error_check() reports BM_ERR_CAPACITY. */
 size_t bm_nl_workspace_bytes(int64_t N, const float* box_host, double cutoff);
 int bm_nl_count(const float* pos, int64_t N, const float* box_host, double cutoff, bool self_loops,
                 int64_t* row_ptr, void* workspace, size_t workspace_bytes, void* stream);

@@ -1,7 +1,8 @@
 #!/usr/bin/env python3
 """Regenerate the golden fixtures in this directory from the reference tree.
 
-Needs the reference checkout (default /root/reference) and runs on the CPU:
+Needs the reference checkout (--ref, or the BATMOBILE_REF environment variable)
+and runs on the CPU:
 
 * cg_l3.json   -- the 34-path / 611-entry CG table parsed from the reference's
                   vendored include/cg_coefficients_l3.cuh:23-792 (BLOCK_INFO,
@@ -16,7 +17,7 @@ Needs the reference checkout (default /root/reference) and runs on the CPU:
                   (tests/test_neighbor_list.cu:30-68, via oracle/_ref) on its own
                   mt19937 positions for N = 100 and 300 at density 0.05, rc = 5.
 
-    python tests/golden/gen_golden.py [--ref /root/reference]
+    python tests/golden/gen_golden.py --ref <reference checkout>
 """
 import argparse
 import importlib.util
@@ -95,8 +96,10 @@ def nl_fixture():
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("BATMOBILE_REF"))
     a = ap.parse_args()
+    if not a.ref:
+        ap.error("give --ref <reference checkout> or set BATMOBILE_REF")
     with open(os.path.join(HERE, "cg_l3.json"), "w") as f:
         json.dump(parse_cg(a.ref), f)
     np.savez_compressed(os.path.join(HERE, "sh_ref.npz"), **sh_fixture(a.ref))

@@ -21,7 +21,7 @@ class CpuCompute:
         keep = ei[0] < n_rows
         return ei[1][keep], ei[0][keep], -vec[keep].double(), None
 
-    def layer(self, x_l, vec, W, src, dst, graph, G_l):
+    def layer(self, x_l, vec, W, src, dst, graph, G_l, mark=None):
         from oracle import ref_ops
         n = x_l.shape[0]
         ins = [t.detach().double().clone().requires_grad_(True) for t in (x_l, vec, W)]

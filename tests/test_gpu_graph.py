@@ -79,8 +79,8 @@ def test_neighbor_list_reference_golden(bm):
 
 
 @pytest.mark.parametrize("n,box,rc,self_loops", [
-    (1000, 29.7, 5.0, False),
-    (5000, 44.3, 5.0, False),
+    (1000, 29.7, 5.0, False),      # 1000 atoms, ~20 neighbours
+    (5000, 44.3, 5.0, False),      # 5000 atoms, ~30 neighbours
     (2000, [23.0, 17.5, 31.25], 4.5, True),
     (64, 9.0, 5.0, False),         # box < 2 rc: 3 cells per axis, min-image
     (1, 10.0, 3.0, True),
@@ -130,7 +130,7 @@ def test_neighbor_list_reference_ctypes_abi(bm):
 
 
 def test_neighbor_list_1m_properties(bm):
-    """BASELINE config 5 size: symmetric edge set, count ~30 per atom, vectors within rc."""
+    """1M atoms, L=259: symmetric edge set, count ~30 per atom, vectors within rc."""
     g = torch.Generator().manual_seed(4)
     pos = (torch.rand(1_000_000, 3, generator=g) * 259.0).to(dev)
     ei, vec, rp = bm.neighbor_list(pos, [259.0] * 3, 5.0, return_row_ptr=True)
@@ -242,3 +242,27 @@ def test_neighbor_list_plan_graph_replay(bm):
     rei, rvec, rrp = _bm.neighbor_list(pos.clone(), [box] * 3, rc, return_row_ptr=True)
     assert torch.equal(ei, rei) and torch.equal(vec, rvec) and torch.equal(plan.row_ptr, rrp)
     assert lib_error_free()
+
+
+def test_neighbor_list_fill_short_buffers_flagged_not_overrun(bm):
+    """A fill given fewer edge slots than the count found writes nothing past
+    them and reports BM_ERR_CAPACITY through the device error flag."""
+    from batmobile import _batmobile as _bm
+    from batmobile._lib import lib
+    g = torch.Generator().manual_seed(9)
+    n, box = 600, 18.0
+    pos = (torch.rand(n, 3, generator=g) * box).to(dev)
+    plan = _bm.NeighborListPlan(pos, [box] * 3, 5.0)
+    plan.count()
+    E = plan.num_edges()
+    short, guard = E - 37, 4096
+    ei_buf = torch.full((2 * short + guard,), -7, dtype=torch.int64, device=dev)
+    vec_buf = torch.full((short + guard, 3), -7.0, dtype=torch.float32, device=dev)
+    plan.fill(ei_buf[:2 * short].view(2, short), vec_buf[:short])
+    torch.cuda.synchronize()
+    assert lib.bm_device_error_check() == 4          # BM_ERR_CAPACITY
+    assert lib.bm_device_error_check() == 0          # read and cleared
+    assert bool((ei_buf[2 * short:] == -7).all()) and bool((vec_buf[short:] == -7.0).all())
+    # a full-size fill afterwards is complete and exact
+    ei, vec = bm.neighbor_list(pos, [box] * 3, 5.0)
+    assert ei.shape[1] == E

@@ -40,7 +40,7 @@ def test_layer_forward_backward(bm, oracle, n, box, ci, co):
 
 def test_layer_tf32_mix_within_gate(bm, oracle):
     """Single-pass TF32 channel mixes (bm_set_mix_precision(1)): the fused layer's
-    output and gradients stay inside the north star's tf32 gate, 2e-3."""
+    output and gradients stay inside the 2e-3 tolerance allowed for a tf32 mix."""
     from batmobile._lib import lib
     n, box, ci, co = 1000, 29.7, 64, 64
     pos, x, W = pbc_system(n, box, 5.0, ci, co, 21)
@@ -104,7 +104,7 @@ def test_forces_through_edge_vectors(bm, oracle):
 
 
 def test_layer_config4_properties(bm):
-    """BASELINE config 4 size: linearity in W, determinism, and the sum rule
+    """5000 atoms, C=64 (the benchmarked size): linearity in W, determinism, and the sum rule
     sum_n out = sum_e msg (checked through the unfused kernels)."""
     g = torch.Generator().manual_seed(3)
     n, box = 5000, 44.3

@@ -98,7 +98,7 @@ def test_tp_simple_forward_backward(bm, oracle):
 
 @pytest.mark.parametrize("n,ci,co", [(1000, 32, 64), (257, 8, 16), (33, 5, 7)])
 def test_tp_weighted_forward_backward(bm, oracle, n, ci, co):
-    # BASELINE config 3 shape first; odd channel counts exercise the tile edges
+    # the 1000-atom C_in=32, C_out=64 benchmark shape first; odd channel counts exercise the tile edges
     g = torch.Generator().manual_seed(2)
     x = torch.randn(n, ci, 16, generator=g)
     v = torch.randn(n, 3, generator=g)
@@ -158,3 +158,20 @@ def test_tp_weighted_tf32_mode(bm, oracle):
     err = relerr(out, ref)
     assert 1e-6 < err < 2e-3
     assert relerr(bm.tensor_product(x.to(dev), Y.to(dev), W.to(dev)), ref) < TOL
+
+
+def test_bounded_device_wait_times_out_cleanly(bm, oracle):
+    """A device wait that can never complete gives up within its limit, reports
+    BM_ERR_TIMEOUT through the error flag, and the next call runs normally."""
+    import ctypes
+    import time
+    from batmobile._lib import lib
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    t0 = time.monotonic()
+    assert lib.bm_selftest_wait_timeout(st) == 6   # BM_ERR_TIMEOUT
+    assert time.monotonic() - t0 < 10.0
+    assert lib.bm_device_error_check() == 0        # read and cleared
+    v = torch.randn(1000, 3, device="cuda")
+    v = v / v.norm(dim=1, keepdim=True)
+    Y = bm.spherical_harmonics(v, 3)
+    assert relerr(Y, oracle.sh(v.double().cpu(), 3)) < 1e-5
