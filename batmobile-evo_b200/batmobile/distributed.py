@@ -293,10 +293,9 @@ class SlabDecomposition:
             self._deadline_wait(works, "reverse halo")
         out = []
         for gown, (ret_left, ret_right) in zip(grads_owned, rets):
-            o = gown.clone()
-            o.index_add_(0, h.send_left, ret_left)
-            o.index_add_(0, h.send_right, ret_right)
-            out.append(o)
+            gown.index_add_(0, h.send_left, ret_left)    # in place: the owned rows of the step's own gradient
+            gown.index_add_(0, h.send_right, ret_right)
+            out.append(gown)
         return out
 
     def allreduce_sum(self, t: torch.Tensor, block: bool = True) -> torch.Tensor:
@@ -342,8 +341,8 @@ class SlabDecomposition:
         else:
             x_l = x_own
         mark("halo_features")
-        G_l = torch.cat([G_own, G_own.new_zeros((pos_l.shape[0] - n_own,) + tuple(G_own.shape[1:]))], 0)
-        out_l, gx_l, gv, gW = compute.layer(x_l, vec, W, src, dst, graph, G_l, mark)
+        # the upstream gradient exists for the owned rows only (ghost rows are not targets)
+        out_l, gx_l, gv, gW = compute.layer(x_l, vec, W, src, dst, graph, G_own, mark)
         gpos_l = compute.pos_grad(gv, src, dst, graph, pos_l.shape[0])
         mark("pos_grad")
         gW = self.allreduce_sum(gW, block=False)
@@ -370,17 +369,18 @@ class GpuCompute:
         graph = (rp, ident, rps, ps, int(n_rows))
         return src, dst, (-vec).contiguous(), graph
 
-    def layer(self, x_l, vec, W, src, dst, graph, G_l, mark=lambda name: None):
+    def layer(self, x_l, vec, W, src, dst, graph, G_own, mark=lambda name: None):
         """Owned atoms (the first n_rows) are the only targets: the forward, the
         slot gradients and the weight gradient skip the ghost rows; ghosts stay
-        sources, so grad_x covers every local atom.  Returns out for the owned rows."""
+        sources, so grad_x covers every local atom.  G_own: upstream gradient of
+        the owned rows.  Returns out for the owned rows."""
         from . import _batmobile as _bm
         rp, ident, rps, ps, n_own = graph
         rpt = rp[:n_own + 1]
         out, slots = _bm.layer_forward(x_l.contiguous(), vec, W, src, rpt, ident, n_targets=n_own)
         mark("layer_fwd")
         gx, gv, gw = _bm.layer_backward(x_l.contiguous(), vec, W, src, dst, rpt, ident, rps, ps, slots,
-                                        G_l[:n_own].contiguous(), n_targets=n_own)
+                                        G_own.contiguous(), n_targets=n_own)
         mark("layer_bwd")
         return out, gx, gv, gw
 

@@ -137,31 +137,30 @@ static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) =
 // Reverse-edge index of a symmetric CSR whose rows are sorted: for the entry k
 // of row i holding column j, rev[k] = position of i inside row j (binary
 // search).  rev is then the target-grouped permutation of the edge list
-// (row_ptr serves both orders), and rev[rev[k]] == k.  A missing reverse edge
+// (row_ptr serves both orders), and rev[rev[k]] == k.  One warp per row, so
+// the row of an entry is known without a search; a missing reverse edge
 // writes -1 and raises the device error flag.
 __global__ void csr_reverse_kernel(const int64_t* __restrict__ row_ptr, const int64_t* __restrict__ col, int64_t N,
-                                   int64_t E, int64_t* __restrict__ rev, int* err) {
-  const int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (k >= E) return;
-  const int64_t j = col[k];
-  // row of entry k: largest i with row_ptr[i] <= k
-  int64_t lo = 0, hi = N;
-  while (hi - lo > 1) {
-    const int64_t mid = (lo + hi) >> 1;
-    if (row_ptr[mid] <= k) lo = mid; else hi = mid;
-  }
-  const int64_t i = lo;
-  int64_t r = -1;
-  if (j >= 0 && j < N) {
-    int64_t a = row_ptr[j], b = row_ptr[j + 1];
-    while (a < b) {
-      const int64_t mid = (a + b) >> 1;
-      if (col[mid] < i) a = mid + 1; else b = mid;
+                                   int64_t* __restrict__ rev, int* err) {
+  const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (i >= N) return;
+  const int64_t kb = row_ptr[i], ke = row_ptr[i + 1];
+  for (int64_t k = kb + lane; k < ke; k += 32) {
+    const int64_t j = col[k];
+    int64_t r = -1;
+    if (j >= 0 && j < N) {
+      int64_t a = row_ptr[j], b = row_ptr[j + 1];
+      const int64_t end = b;
+      while (a < b) {
+        const int64_t mid = (a + b) >> 1;
+        if (col[mid] < i) a = mid + 1; else b = mid;
+      }
+      if (a < end && col[a] == i) r = a;
     }
-    if (a < row_ptr[j + 1] && col[a] == i) r = a;
+    rev[k] = r;
+    if (r < 0) atomicOr(err, 2);
   }
-  rev[k] = r;
-  if (r < 0) atomicOr(err, 2);
 }
 
 }  // namespace bm
@@ -208,7 +207,7 @@ int bm_csr_reverse(const int64_t* row_ptr, const int64_t* col, int64_t N, int64_
   BM_REQUIRE(row_ptr && col && rev, "csr_reverse: null pointer");
   int* err = tc::error_flag();
   if (!err) return set_error(BM_ERR_CUDA, "csr_reverse: device error flag unavailable");
-  csr_reverse_kernel<<<grid_for(E, 256), 256, 0, as_stream(stream)>>>(row_ptr, col, N, E, rev, err);
+  csr_reverse_kernel<<<grid_for(N * 32, 256), 256, 0, as_stream(stream)>>>(row_ptr, col, N, rev, err);
   return check_launch("csr_reverse");
 }
 

@@ -124,17 +124,19 @@ __global__ void pack_weights_kernel(const float* __restrict__ W, int Ci, int Co,
   if (i >= a.off[4]) return;
   int g = 0;
   while (g < 3 && i >= a.off[g + 1]) ++g;
-  const int64_t j = i - a.off[g];
-  const int CPi = (Ci + 3) & ~3, CPo = (Co + 3) & ~3, P = a.P[g];
+  // every packed group holds fewer than 2^32 entries (checked by pack_weights),
+  // so the index arithmetic below runs in 32 bits
+  const unsigned j = (unsigned)(i - a.off[g]);
+  const unsigned CPi = (Ci + 3) & ~3, CPo = (Co + 3) & ~3, P = a.P[g];
   int pos, ci, co;
   if (mode == kPackFwd) {          // [co][pos*CPi + ci]
-    const int64_t row = j / (P * CPi), col = j - row * (P * CPi);
+    const unsigned row = j / (P * CPi), col = j - row * (P * CPi);
     co = (int)row; pos = (int)(col / CPi); ci = (int)(col - pos * CPi);
   } else if (mode == kPackDx) {    // [ci][pos*CPo + co]
-    const int64_t row = j / (P * CPo), col = j - row * (P * CPo);
+    const unsigned row = j / (P * CPo), col = j - row * (P * CPo);
     ci = (int)row; pos = (int)(col / CPo); co = (int)(col - pos * CPo);
   } else {                         // [pos*CPi + ci][co]
-    const int64_t row = j / CPo;
+    const unsigned row = j / CPo;
     co = (int)(j - row * CPo); pos = (int)(row / CPi); ci = (int)(row - pos * CPi);
   }
   out[i] = (ci < Ci && co < Co) ? W[((int64_t)a.path[g][pos] * Ci + ci) * Co + co] : 0.0f;
@@ -147,6 +149,8 @@ int pack_weights(const float* W, int Ci, int Co, int mode, float* out, cudaStrea
     for (int i = 0; i < 11; ++i) a.path[g][i] = mode == kPackDx ? kL1Group[g][i] : kLoGroup[g][i];
   }
   for (int g = 0; g <= 4; ++g) a.off[g] = pack_group_offset(mode, g, Ci, Co);
+  for (int g = 0; g < 4; ++g)
+    BM_REQUIRE(a.off[g + 1] - a.off[g] < (int64_t(1) << 32), "pack_weights: C_in = %d, C_out = %d too large", Ci, Co);
   pack_weights_kernel<<<grid_for(a.off[4], 256), 256, 0, st>>>(W, Ci, Co, mode, a, out);
   return check_launch("pack_weights");
 }

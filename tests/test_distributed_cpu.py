@@ -21,9 +21,10 @@ class CpuCompute:
         keep = ei[0] < n_rows
         return ei[1][keep], ei[0][keep], -vec[keep].double(), None
 
-    def layer(self, x_l, vec, W, src, dst, graph, G_l, mark=None):
+    def layer(self, x_l, vec, W, src, dst, graph, G_own, mark=None):
         from oracle import ref_ops
         n = x_l.shape[0]
+        G_l = torch.cat([G_own, G_own.new_zeros((n - G_own.shape[0],) + tuple(G_own.shape[1:]))], 0)
         ins = [t.detach().double().clone().requires_grad_(True) for t in (x_l, vec, W)]
         out = ref_ops.interaction(ins[0], ins[1], ins[2], torch.stack([src, dst]), n)
         gx, gv, gw = torch.autograd.grad(out, ins, G_l.double())

@@ -19,8 +19,11 @@ def pbc_system(n, box, rc, ci, co, seed):
     return pos, x, W
 
 
-@pytest.mark.parametrize("n,box,ci,co", [(200, 15.0, 16, 16), (1000, 29.7, 32, 32), (300, 18.0, 70, 20)])
+@pytest.mark.parametrize("n,box,ci,co", [(200, 15.0, 16, 16), (1000, 29.7, 32, 32), (300, 18.0, 70, 20),
+                                         (500, 10.0, 7, 9), (160, 12.0, 33, 5)])
 def test_layer_forward_backward(bm, oracle, n, box, ci, co):
+    """Includes odd channel counts and, at 500 atoms in a 10 A box, atoms with
+    more than 250 incoming edges."""
     pos, x, W = pbc_system(n, box, 5.0, ci, co, n)
     ei, vec = bm.neighbor_list(pos.to(dev), [box] * 3, 5.0)
     xg = x.to(dev).requires_grad_(True)
@@ -210,7 +213,7 @@ def test_gpu_compute_owned_targets_matches_full(bm):
     G_l = G[order].to(dev)
     G_l[n_own:] = 0
     src, dst, vec, graph = comp.neighbors(pos_l, n_own, [box] * 3, rc)
-    out, gx, gv, gw = comp.layer(x_l, vec, W.to(dev), src, dst, graph, G_l)
+    out, gx, gv, gw = comp.layer(x_l, vec, W.to(dev), src, dst, graph, G_l[:n_own].contiguous())
     gp = comp.pos_grad(gv, src, dst, graph, n)
     Gm = G.clone()
     Gm[~owned] = 0
@@ -226,3 +229,4 @@ def test_gpu_compute_owned_targets_matches_full(bm):
     assert relerr(out, ref[od[:n_own]]) < 1e-6
     assert relerr(gx, rgx[od]) < 1e-6 and relerr(gw, rgw) < 1e-6
     assert relerr(gp, rgp[od]) < 1e-5
+
