@@ -361,10 +361,34 @@ def cpu_reference_step(x, v, W, ei, n, Gs, sample_atoms):
     return int(eis.shape[1])
 
 
-def cpu_baseline(x, v, W, ei, G, n, budget_s=15.0):
+def cpu_full_step(pos, x, W, G, cfg):
+    """The whole step on the host: neighbour list (the C cell list of the
+    reference's brute-force predicate, one thread) + the reference
+    formulation's forward and autograd backward over every edge, fp32."""
+    from oracle import ref_ops
+    t0 = time.perf_counter()
+    ei, v = ref_ops.nl_cells(pos, [cfg["box"]] * 3, cfg["rc"])
+    t_nl = time.perf_counter() - t0
+    vs = v.clone().requires_grad_(True)
+    xs = x.clone().requires_grad_(True)
+    Ws = W.clone().requires_grad_(True)
+    out = ref_ops.interaction_chunked(xs, vs, Ws, ei, cfg["n"], chunk=16384)
+    out.backward(G)
+    return int(ei.shape[1]), t_nl, time.perf_counter() - t0
+
+
+def cpu_baseline(x, v, W, ei, G, n, budget_s=15.0, pos=None, cfg=None):
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     xc, vc, Wc, eic, Gc = x.cpu(), v.cpu(), W.cpu(), ei.cpu(), G.cpu()
+    if pos is not None:
+        cpu_reference_step(xc, vc, Wc, eic, n, Gc, 250)  # warm-up on a sample
+        edges, t_nl, t = cpu_full_step(pos.cpu(), xc, Wc, Gc, cfg)
+        return {"value": edges / t / 1e6, "unit": "Medges/s", "cores": threads, "kind": "port",
+                "ms_per_step": t * 1e3, "neighbor_list_ms": t_nl * 1e3,
+                "sample": "the full step, one run: neighbour list (oracle C cell list, 1 thread) + reference PyTorch "
+                          "formulation (oracle/ref_ops.interaction_chunked, fp32) forward + autograd backward "
+                          "w.r.t. x, W, edge vectors over all %d edges" % edges}
     sample = 250
     t0 = time.perf_counter()
     edges = cpu_reference_step(xc, vc, Wc, eic, n, Gc, sample)  # warm-up
@@ -844,7 +868,7 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import ref_ops  # noqa: F401  (CPU baseline leg only)
         ei, vec = _bm.neighbor_list(pos, [CFG["box"]] * 3, CFG["rc"])
-        cpu = cpu_baseline(x_h, vec.cpu(), W_h, ei.cpu(), G_h, n)
+        cpu = cpu_baseline(x_h, vec.cpu(), W_h, ei.cpu(), G_h, n, pos=pos_h, cfg=CFG)
     ref_cuda_row = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         # comparison arm: the reference's own CUDA kernels, compiled for sm_100a
