@@ -1113,3 +1113,13 @@ int bm_layer_bwd_targets(const float* x, const float* v, const float* W, const i
 }
 
 }  // extern "C"
+
+#ifdef BM_DIAG
+extern "C" __attribute__((visibility("default"))) int bm_gdiag_read(unsigned long long* out) {
+  cudaDeviceSynchronize();
+  cudaMemcpyFromSymbol(out, bm::tc::g_gdiag, sizeof(unsigned long long) * 16);
+  unsigned long long z[16] = {0};
+  cudaMemcpyToSymbol(bm::tc::g_gdiag, z, sizeof(z));
+  return 0;
+}
+#endif

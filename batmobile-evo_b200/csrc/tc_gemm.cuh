@@ -158,6 +158,19 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
 
 constexpr int kBM = 128, kBK = 32;
 
+#ifdef BM_DIAG
+static __device__ unsigned long long g_gdiag[16];
+#define GD_DECL unsigned long long gd[16] = {0}; unsigned long long gt0 = clock64(), gts = gt0;
+#define GD_MARK() gt0 = clock64();
+#define GD_ADD(slot) { unsigned long long _n = clock64(); gd[slot] += _n - gt0; gt0 = _n; }
+#define GD_FLUSH(tslot) if (lane == 0) { gd[tslot] = clock64() - gts; for (int _i = 0; _i < 16; ++_i) atomicAdd(&g_gdiag[_i], gd[_i]); }
+#else
+#define GD_DECL
+#define GD_MARK()
+#define GD_ADD(slot)
+#define GD_FLUSH(tslot)
+#endif
+
 // --------------------------------------------------------------------------
 // Persistent, warp-specialised kernel.  Roles (320 threads):
 //   warp 0      TMA: one lane waits for a free ring slot, arms full[slot] with
@@ -398,6 +411,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) tc_gemm_kernel(const __grid_con
   if (warp == 0) {
     // ----------------------------------------------------------------- TMA
     int slab = 0;
+    GD_DECL
     if (lane == 0) {
       for (int id = blockIdx.x; id < G.total && ok; id += gridDim.x) {
         const TileInfo ti = tile_info<P, BN>(G, id);
@@ -405,7 +419,9 @@ __global__ void __launch_bounds__(kWsThreads, 1) tc_gemm_kernel(const __grid_con
         const CUtensorMap* mb = &G.tb[ti.g];
         for (int kb = 0; kb < ti.nk && ok; ++kb, ++slab) {
           const int s = slab % S;
+          GD_ADD(1)
           if (slab >= S) ok = mbar_wait(&empty[s], ((slab / S) - 1) & 1, err);
+          GD_ADD(0)
           if (!ok) break;
           const uint32_t st = sbase + s * L::kStage;
           const int64_t k0 = ti.kbeg + (int64_t)kb * kBK;
@@ -416,7 +432,9 @@ __global__ void __launch_bounds__(kWsThreads, 1) tc_gemm_kernel(const __grid_con
       }
       // copies still in flight land before the CTA may exit (bounded)
       for (int j = slab - S > 0 ? slab - S : 0; j < slab; ++j) mbar_wait(&full[j % S], (j / S) & 1, nullptr);
+      GD_ADD(1)
     }
+    GD_FLUSH(15)
     __syncwarp();
   } else if (warp <= kSplitWarps) {
     // --------------------------------------------------------------- split
@@ -426,11 +444,14 @@ __global__ void __launch_bounds__(kWsThreads, 1) tc_gemm_kernel(const __grid_con
       const int row = quarter * 32 + lane;
       const int st_t = t - 32;  // 0..127 over the B split
       int slab = 0;
+      GD_DECL
       for (int id = blockIdx.x; id < G.total && ok; id += gridDim.x) {
         const TileInfo ti = tile_info<P, BN>(G, id);
         for (int kb = 0; kb < ti.nk && ok; ++kb, ++slab) {
           const int s = slab % S;
+          GD_ADD(3)
           ok = mbar_wait(&full[s], (slab / S) & 1, err);
+          GD_ADD(2)
           if (!ok) break;
           const uint8_t* st = smem + s * L::kStage;
           float v[32];
@@ -453,21 +474,28 @@ __global__ void __launch_bounds__(kWsThreads, 1) tc_gemm_kernel(const __grid_con
           if (lane == 0) mbar_arrive(&ready[s]);
         }
       }
+      GD_ADD(3)
+      if (warp == 1) { GD_FLUSH(14) }
     }
   } else if (warp == kMmaWarp) {
     // ----------------------------------------------------------------- MMA
     constexpr uint32_t idesc = idesc_tf32(kBM, BN, P::kAMN ? 1 : 0, P::kBMN ? 1 : 0);
     constexpr uint32_t idesc_t = idesc_tf32(kBM, BN, 0, P::kBMN ? 1 : 0);  // A from TMEM (lane = row)
     int slab = 0, tcount = 0;
+    GD_DECL
     for (int id = blockIdx.x; id < G.total && ok; id += gridDim.x, ++tcount) {
       const TileInfo ti = tile_info<P, BN>(G, id);
       const int ab = tcount & 1;
+      GD_ADD(6)
       if (tcount >= 2) ok = mbar_wait(&tempty[ab], ((tcount >> 1) - 1) & 1, err) && ok;
+      GD_ADD(7)
       tc_fence_after();
       const uint32_t dacc = tmem + (uint32_t)(ab * BN);
       for (int kb = 0; kb < ti.nk && ok; ++kb, ++slab) {
         const int s = slab % S;
+        GD_ADD(6)
         ok = mbar_wait(kSplit3 ? &ready[s] : &full[s], (slab / S) & 1, err) && ok;
+        GD_ADD(4)
         tc_fence_after();
         if (lane == 0 && ok) {
           const uint32_t a_sm = sbase + s * L::kStage, b_hi = a_sm + L::kA, b_lo = b_hi + L::kB;
@@ -491,16 +519,21 @@ __global__ void __launch_bounds__(kWsThreads, 1) tc_gemm_kernel(const __grid_con
       if (ti.nk == 0 && lane == 0) mma_commit(&tfull[ab]);  // nothing issued: signal at once
       __syncwarp();
     }
+    GD_ADD(6)
+    GD_FLUSH(13)
   } else {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     int tcount = 0;
+    GD_DECL
     for (int id = blockIdx.x; id < G.total && ok; id += gridDim.x, ++tcount) {
       const TileInfo ti = tile_info<P, BN>(G, id);
       const P& p = G.p[ti.g];
       const int ab = tcount & 1;
+      GD_ADD(9)
       ok = mbar_wait(&tfull[ab], (tcount >> 1) & 1, err) && ok;
+      GD_ADD(8)
       ok = __all_sync(0xffffffffu, ok);
       tc_fence_after();
       if constexpr (P::kTmaStore) {
@@ -550,6 +583,8 @@ __global__ void __launch_bounds__(kWsThreads, 1) tc_gemm_kernel(const __grid_con
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[ab]);  // TMEM buffer free for the tile after next
     }
+    GD_ADD(9)
+    if (warp == kMmaWarp + 1) { GD_FLUSH(12) }
     if constexpr (P::kTmaStore) {
       if (t == (kMmaWarp + 1) * 32) bulk_wait0();  // stores complete before the CTA exits
     }
