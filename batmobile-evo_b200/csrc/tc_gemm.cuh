@@ -213,8 +213,13 @@ struct Smem {
   static constexpr int kEpiStage = kTmaStore ? kBM * 128 : 0;
   static constexpr int kBudget = 216 * 1024 - kEpiStage;
   static constexpr int kFit = kBudget / kStage;
-  // kSplit3: TMEM holds 2 accumulators (2 BN columns) + per stage A hi and lo (64 columns)
-  static constexpr int kTmemFit = kSplit3 ? (512 - 2 * BN) / 64 : kMaxStages;
+  // kSplit3 with BN = 64 fuses two of the three products into one N = 128 MMA
+  // (A_hi x [B_hi | B_lo]) and accumulates A_lo x B_hi into its second half, so
+  // an accumulator is 2 BN columns wide; the epilogue adds the two halves.
+  static constexpr bool kFuse = kSplit3 && BN == 64;
+  static constexpr int kAccCols = kFuse ? 2 * BN : BN;
+  // kSplit3: TMEM holds 2 accumulators + per stage A hi and lo (64 columns)
+  static constexpr int kTmemFit = kSplit3 ? (512 - 2 * kAccCols) / 64 : kMaxStages;
   static constexpr int kFit2 = kFit < kTmemFit ? kFit : kTmemFit;
   static constexpr int kStages = kFit2 > kMaxStages ? kMaxStages : kFit2;
   static constexpr int kBytes = kStages * kStage + kEpiStage + 1024;  // + alignment slack
@@ -456,7 +461,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) tc_gemm_kernel(const __grid_con
           const uint8_t* st = smem + s * L::kStage;
           float v[32];
           load_a_row<P::kAMN>(st, row, v);
-          const uint32_t ta = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(2 * BN + s * 64);
+          const uint32_t ta = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(2 * L::kAccCols + s * 64);
           tmem_st32(ta, v);
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = tf32_lo(v[j]);
@@ -490,7 +495,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) tc_gemm_kernel(const __grid_con
       if (tcount >= 2) ok = mbar_wait(&tempty[ab], ((tcount >> 1) - 1) & 1, err) && ok;
       GD_ADD(7)
       tc_fence_after();
-      const uint32_t dacc = tmem + (uint32_t)(ab * BN);
+      const uint32_t dacc = tmem + (uint32_t)(ab * L::kAccCols);
       for (int kb = 0; kb < ti.nk && ok; ++kb, ++slab) {
         const int s = slab % S;
         GD_ADD(6)
@@ -499,11 +504,16 @@ __global__ void __launch_bounds__(kWsThreads, 1) tc_gemm_kernel(const __grid_con
         tc_fence_after();
         if (lane == 0 && ok) {
           const uint32_t a_sm = sbase + s * L::kStage, b_hi = a_sm + L::kA, b_lo = b_hi + L::kB;
-          const uint32_t a_tm = tmem + (uint32_t)(2 * BN + s * 64);  // A hi; lo 32 columns on
+          const uint32_t a_tm = tmem + (uint32_t)(2 * L::kAccCols + s * 64);  // A hi; lo 32 columns on
 #pragma unroll
           for (int kk = 0; kk < kBK / 8; ++kk) {
             const uint64_t bd = op_desc<BN, P::kBMN>(b_hi, kk);
-            if (kSplit3) {
+            if constexpr (L::kFuse) {
+              // B lo sits right after B hi: one N = 2 BN operand [B_hi | B_lo]
+              constexpr uint32_t idesc_f = idesc_tf32(kBM, 2 * BN, 0, P::kBMN ? 1 : 0);
+              mma_tf32_ta(dacc, a_tm + kk * 8, bd, idesc_f, (kb > 0 || kk > 0) ? 1u : 0u);
+              mma_tf32_ta(dacc + BN, a_tm + 32 + kk * 8, bd, idesc_t, 1u);
+            } else if (kSplit3) {
               mma_tf32_ta(dacc, a_tm + kk * 8, bd, idesc_t, (kb > 0 || kk > 0) ? 1u : 0u);
               mma_tf32_ta(dacc, a_tm + kk * 8, op_desc<BN, P::kBMN>(b_lo, kk), idesc_t, 1u);
               mma_tf32_ta(dacc, a_tm + 32 + kk * 8, bd, idesc_t, 1u);
@@ -545,8 +555,16 @@ __global__ void __launch_bounds__(kWsThreads, 1) tc_gemm_kernel(const __grid_con
         for (int c0 = 0; c0 < BN; c0 += 32) {
           float v[32];
           if (ti.nk > 0 && ok) {
-            tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(ab * BN + c0), v);
-            tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(ab * BN + c0 + 16), v + 16);
+            const uint32_t tb = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(ab * L::kAccCols + c0);
+            tmem_ld16(tb, v);
+            tmem_ld16(tb + 16, v + 16);
+            if constexpr (L::kFuse) {
+              float w[32];
+              tmem_ld16(tb + BN, w);
+              tmem_ld16(tb + BN + 16, w + 16);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] += w[j];
+            }
           } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = 0.0f;
@@ -570,7 +588,14 @@ __global__ void __launch_bounds__(kWsThreads, 1) tc_gemm_kernel(const __grid_con
         for (int c0 = 0; c0 < BN; c0 += 16) {
           float v[16];
           if (ti.nk > 0 && ok) {
-            tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(ab * BN + c0), v);
+            const uint32_t tb = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(ab * L::kAccCols + c0);
+            tmem_ld16(tb, v);
+            if constexpr (L::kFuse) {
+              float w[16];
+              tmem_ld16(tb + BN, w);
+#pragma unroll
+              for (int j = 0; j < 16; ++j) v[j] += w[j];
+            }
           } else {
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] = 0.0f;

@@ -6,11 +6,11 @@ forward -> backward (grads w.r.t. node features, weights and, through the edge
 vectors, positions).  Workload: N=5000 atoms uniform in a periodic cube of side
 44.3 A, cutoff 5 A (~150k edges), C=64, fp32, seed 3 (torch.manual_seed(3);
 pos = rand(N,3)*L, W = randn(34,C,C)/sqrt(C), x = randn(N,C,16), upstream
-grad = randn(N,C,16)), synthetic data.  The step runs as CUDA graphs around
-the one host read of the edge count: the neighbour-list count, then (captured
-once per edge count) the neighbour-list fill and CSR views, and the layer
-forward, backward and position gradient; every replay recomputes everything
-from the current inputs, without host gaps between launches.
+grad = randn(N,C,16)), synthetic data.  The step runs as two CUDA graphs with no
+host read inside the step: the neighbour list (count and fill into edge
+buffers sized once, with headroom, from the first count) with the CSR views,
+and the layer forward, backward and position gradient; every replay
+recomputes everything from the current inputs.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
@@ -174,25 +174,36 @@ def gpu_step(bm, _bm, pos, x, W, G, cfg, stages=None, lib=None, x_ready=None):
 
 
 class GraphedStep:
-    """The config-4 step as CUDA graphs around the one host read it needs.
-    Graph A (captured once): the neighbour-list count over the static positions
-    (binning, per-atom counts, row offsets).  Then the host reads the edge
-    count E.  Captured once per E: graph B1, the neighbour-list fill into static
-    edge buffers and the CSR views (no node features needed, so it runs while
-    they are still being copied in), and graph B2, the layer forward, backward
-    and the position gradient.  Every replay recomputes everything from the
-    current contents of the static inputs (positions, node features, weights,
-    upstream gradient)."""
+    """The 5000-atom step as two CUDA graphs with no host read between them.
+    Set-up (once): the neighbour-list count and one host read of the edge
+    count E, which sizes static edge buffers with headroom (capacity).  Graph
+    A: the neighbour-list count and fill into the capacity buffers and the CSR
+    views (it needs no node features, so end to end it runs while they are
+    still being copied in); graph B: the layer forward, backward and the
+    position gradient.  Every replay recomputes everything from the current
+    contents of the static inputs (positions, node features, weights, upstream
+    gradient); the kernels walk the CSR offsets the replay computed, so only the
+    first E slots of the buffers are touched.  A list longer than the capacity
+    sets the device error flag (the fill drops what does not fit); `check()`
+    reads it and `edges()` reads E, both outside the timed region."""
 
-    def __init__(self, bm, _bm, lib, cfg, pos, x, W, G):
+    def __init__(self, bm, _bm, lib, cfg, pos, x, W, G, headroom=0.125):
         self.bm, self._bm, self.lib, self.cfg = bm, _bm, lib, cfg
         self.pos, self.x, self.W, self.G = pos, x, W, G
         self.plan = _bm.NeighborListPlan(pos, [cfg["box"]] * 3, cfg["rc"])
-        self.graph_a = self._capture(self.plan.count)
-        self.launches_a = self._captured_launches
-        self.E = None
-        self.graph_b1 = self.graph_b2 = None
-        self.launches_b = 0
+        self.plan.count()
+        self.E = self.plan.num_edges()
+        cap = self.E + int(self.E * headroom) + 1024
+        dev = pos.device
+        self.ei = torch.empty(2, cap, dtype=torch.int64, device=dev)
+        self.vec = torch.empty(cap, 3, dtype=torch.float32, device=dev)
+        self.capacity = cap
+        self.graph_a = self._capture(self._edges)
+        self.graph = self._out
+        self.launches = self._captured_launches
+        self.graph_b = self._capture(self._layer)
+        self.launches += self._captured_launches
+        self.outputs = self._out
 
     def _capture(self, fn):
         side = torch.cuda.Stream()
@@ -210,6 +221,7 @@ class GraphedStep:
         return g
 
     def _edges(self):
+        self.plan.count()
         self.plan.fill(self.ei, self.vec)
         graph = self.bm.EdgeGraph(self.ei, self.cfg["n"], src_row_ptr=self.plan.row_ptr, symmetric=True)
         graph.src_csr  # builds the source-grouped view inside this graph
@@ -226,30 +238,26 @@ class GraphedStep:
 
     def __call__(self, x_ready=None):
         self.graph_a.replay()
-        E = self.plan.num_edges()
-        if E != self.E:
-            dev = self.pos.device
-            self.ei = torch.empty(2, E, dtype=torch.int64, device=dev)
-            self.vec = torch.empty(E, 3, dtype=torch.float32, device=dev)
-            if x_ready is not None:
-                torch.cuda.current_stream().wait_event(x_ready)
-            self.graph_b1 = self._capture(self._edges)
-            self.graph = self._out
-            n1 = self._captured_launches
-            self.graph_b2 = self._capture(self._layer)
-            self.launches_b = n1 + self._captured_launches
-            self.outputs = self._out
-            self.E = E
-        self.graph_b1.replay()
         if x_ready is not None:  # node features copied in on a side stream meanwhile
             torch.cuda.current_stream().wait_event(x_ready)
-        self.graph_b2.replay()
+        self.graph_b.replay()
         out, gx, gw, gpos = self.outputs
-        return out, gx, gw, gpos, E
+        return out, gx, gw, gpos, self.E
 
-    @property
-    def launches(self):
-        return self.launches_a + self.launches_b
+    def edges(self):
+        """E of the last replay (a host read)."""
+        return self.plan.num_edges()
+
+    def check(self):
+        """Raises if a replay's list did not fit the capacity (or a device wait timed out)."""
+        torch.cuda.synchronize()
+        rc = self.lib.bm_device_error_check()
+        if rc != 0:
+            raise RuntimeError("graphed step: %s (capacity %d edges)" % (self.lib.bm_last_error().decode(),
+                                                                          self.capacity))
+        if self.edges() != self.E:
+            raise RuntimeError("graphed step: the edge count changed (%d -> %d); rebuild the step"
+                               % (self.E, self.edges()))
 
 
 def mace_step_timing(bm, dev, pos, steps, warmup):
@@ -755,6 +763,7 @@ def main():
         step_ms.append(s.elapsed_time(e))
     torch.cuda.synchronize()
     clk.__exit__(None, None, None)
+    step.check()   # every replay's list fitted the edge buffers (outside the timed region)
     barrier(world)
     # library kernels of the two graphs per replay (eager launches, if any, on top)
     launches = lib.bm_launch_count() - launches0 + args.steps * step.launches
@@ -805,6 +814,7 @@ def main():
         e.synchronize()
         if i >= args.warmup:
             e2e_ms.append(s.elapsed_time(e))
+    step.check()
     t_e2e = max_over_ranks(sum(e2e_ms) / len(e2e_ms), world)
     e2e_value = world * E / (t_e2e * 1e-3) / 1e6
 

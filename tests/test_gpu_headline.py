@@ -57,9 +57,10 @@ def test_graphed_step_at_benchmark_size_matches_oracle(bm, oracle, bench_mod):
     for a, b in ((out, out2), (gx, gx2), (gw, gw2), (gpos, gpos2)):
         assert torch.equal(a, b)
 
+    step.check()   # the list fitted the step's edge buffers, no device wait timed out
     rei, rvec = oracle.nl_cells(pos_h, [cfg["box"]] * 3, cfg["rc"])
-    assert E == rei.shape[1]
-    assert torch.equal(step.ei.cpu(), rei) and torch.equal(step.vec.cpu(), rvec)
+    assert E == rei.shape[1] == step.edges()
+    assert torch.equal(step.ei[:, :E].cpu(), rei) and torch.equal(step.vec[:E].cpu(), rvec)
 
     xd, vd, Wd = x_h.double(), rvec.double(), W_h.double()
     f = lambda a, b, c: oracle.interaction_hoisted(a, b, c, rei, n)  # noqa: E731
