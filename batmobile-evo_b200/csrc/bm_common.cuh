@@ -51,6 +51,15 @@ __device__ __forceinline__ void ffma2(float2& d, float2 a, float2 b) {
   d.y = __uint_as_float((unsigned)(dd >> 32));
 }
 
+// Packed fp32 pair add (sm_100 f32x2): a + b lane-wise, one instruction.
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  unsigned long long aa = (unsigned long long)__float_as_uint(a.x) | ((unsigned long long)__float_as_uint(a.y) << 32);
+  const unsigned long long bb =
+      (unsigned long long)__float_as_uint(b.x) | ((unsigned long long)__float_as_uint(b.y) << 32);
+  asm("add.rn.f32x2 %0, %0, %1;" : "+l"(aa) : "l"(bb));
+  return make_float2(__uint_as_float((unsigned)aa), __uint_as_float((unsigned)(aa >> 32)));
+}
+
 inline unsigned grid_for(int64_t n, int block) {
   int64_t g = (n + block - 1) / block;
   return (unsigned)(g > 0 ? g : 1);

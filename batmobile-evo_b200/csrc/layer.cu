@@ -720,6 +720,11 @@ layer_target_ws_kernel(const __grid_constant__ CUtensorMap xmap, const float* __
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  // zero the x ring once: rows past C_in are never written by the row copies,
+  // and the edge loop reads every channel row without masking
+  for (int i = t; i < kTBufs * kBatch * kTRowBytes / 16; i += blockDim.x)
+    reinterpret_cast<float4*>(ring)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  tc::fence_proxy_async_smem();
   __syncthreads();
   bool ok = true;
   const uint32_t row_bytes = (uint32_t)Ci * 64u;
@@ -845,6 +850,10 @@ layer_target_ws_kernel(const __grid_constant__ CUtensorMap xmap, const float* __
         }
         if (mq == 0 && je < cnt) {
           const TMeta mm = meta[buf * kBatch + je];
+          if (!mm.valid) {  // the ring slot of an invalid source holds stale rows
+#pragma unroll
+            for (int m2 = 0; m2 < 16; ++m2) dyv[m2] = 0.0f;
+          }
           target_edge_epilogue(mm.e, mm.vx, mm.vy, mm.vz, mm.sc, dyv, gv, gscale);
         }
         __syncwarp();
@@ -859,8 +868,9 @@ layer_target_ws_kernel(const __grid_constant__ CUtensorMap xmap, const float* __
     float4* tile = dbt;
     // edge-loop mapping: warp w owns channels 8w .. 8w+7, lane = (channel, m2 quarter)
     const int qq = lane & 3, ce = 8 * warp + (lane >> 2);
-    const bool cev = ce < Ci;
     const int sw = (ce >> 1) & 3;  // 64-byte swizzle of channel row ce
+    const bool hi16 = lane & 16, h8 = lane & 8;
+    const int red_m2 = 4 * qq + (hi16 ? 2 : 0) + (h8 ? 1 : 0);  // m2 this lane's reduced value belongs to
     uint32_t bi = 0, ac = 0;
     bool stuck = false;  // a bounded wait of this warp gave up in the edge loop (warp-uniform)
     for (int64_t n = blockIdx.x; n < N && ok; n += gridDim.x) {
@@ -884,12 +894,19 @@ layer_target_ws_kernel(const __grid_constant__ CUtensorMap xmap, const float* __
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&dempty);
       consumer_sync();
-      float2 d2[8][4];  // [m1 pair][m2 within the quarter]
+      // d2[p][j] = (dB[ce, 2p, m], dB[ce, 2p+1, m]) with m = 4 qq + (j ^ xo): the lane's
+      // m2 order is permuted by its reduce-scatter position, so that every lane
+      // keeps local {0, 1} and sends {2, 3} at the first shuffle stage and keeps
+      // 0, sends 1 at the second (no lane-dependent selects in the edge loop)
+      float2 d2[8][4];
 #pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        const float4 v = *dbt_chunk(tile, ce, qq, k);
-        d2[k >> 1][2 * (k & 1)] = make_float2(v.x, v.y);
-        d2[k >> 1][2 * (k & 1) + 1] = make_float2(v.z, v.w);
+      for (int p = 0; p < 8; ++p) {
+        const float4 lo = *dbt_chunk(tile, ce, qq, 2 * p + (hi16 ? 1 : 0));  // local j = 0, 1
+        const float4 up = *dbt_chunk(tile, ce, qq, 2 * p + (hi16 ? 0 : 1));  // local j = 2, 3
+        d2[p][0] = h8 ? make_float2(lo.z, lo.w) : make_float2(lo.x, lo.y);
+        d2[p][1] = h8 ? make_float2(lo.x, lo.y) : make_float2(lo.z, lo.w);
+        d2[p][2] = h8 ? make_float2(up.z, up.w) : make_float2(up.x, up.y);
+        d2[p][3] = h8 ? make_float2(up.x, up.y) : make_float2(up.z, up.w);
       }
       for (int64_t e0 = eb; e0 < ee && !stuck; e0 += kBatch, ++bi) {
         const int cnt = (int)imin64(kBatch, ee - e0);
@@ -901,11 +918,13 @@ layer_target_ws_kernel(const __grid_constant__ CUtensorMap xmap, const float* __
           stuck = true;
           break;
         }
+        const uint8_t* row0 = ring + (size_t)(buf * kBatch) * kTRowBytes + ce * 64;
+        float* rdst = &red[par][0][warp][red_m2];
 #pragma unroll 2
         for (int j = 0; j < cnt; ++j) {
-          const int sl = buf * kBatch + j;
-          const bool xv = cev && meta[sl].valid;
-          const uint8_t* row = ring + (size_t)sl * kTRowBytes + ce * 64;
+          // rows of invalid sources and channels >= C_in hold finite data (the ring
+          // starts zeroed); the epilogue drops invalid edges, dB is zero past C_in
+          const uint8_t* row = row0 + (size_t)j * kTRowBytes;
           float2 a[2][4];
 #pragma unroll
           for (int h = 0; h < 2; ++h)
@@ -913,8 +932,7 @@ layer_target_ws_kernel(const __grid_constant__ CUtensorMap xmap, const float* __
             for (int m = 0; m < 4; ++m) a[h][m] = make_float2(0.f, 0.f);
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            float4 x4 = *reinterpret_cast<const float4*>(row + ((i ^ sw) << 4));
-            if (!xv) x4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 x4 = *reinterpret_cast<const float4*>(row + ((i ^ sw) << 4));
             const float2 xa = make_float2(x4.x, x4.y), xb = make_float2(x4.z, x4.w);
 #pragma unroll
             for (int m = 0; m < 4; ++m) {
@@ -924,17 +942,16 @@ layer_target_ws_kernel(const __grid_constant__ CUtensorMap xmap, const float* __
           }
           float v[4];
 #pragma unroll
-          for (int m = 0; m < 4; ++m) v[m] = (a[0][m].x + a[0][m].y) + (a[1][m].x + a[1][m].y);
+          for (int m = 0; m < 4; ++m) {
+            const float2 s2 = fadd2(a[0][m], a[1][m]);
+            v[m] = s2.x + s2.y;
+          }
           // reduce-scatter over the warp's 8 channels (lanes with equal qq)
-          const bool hi = lane & 16, h8 = lane & 8;
-          float2 keep = hi ? make_float2(v[2], v[3]) : make_float2(v[0], v[1]);
-          const float2 send = hi ? make_float2(v[0], v[1]) : make_float2(v[2], v[3]);
-          keep.x += __shfl_xor_sync(0xffffffffu, send.x, 16);
-          keep.y += __shfl_xor_sync(0xffffffffu, send.y, 16);
-          float k1 = h8 ? keep.y : keep.x;
-          k1 += __shfl_xor_sync(0xffffffffu, h8 ? keep.x : keep.y, 8);
-          k1 += __shfl_xor_sync(0xffffffffu, k1, 4);
-          if ((lane & 4) == 0) red[par][j][warp][4 * qq + (hi ? 2 : 0) + (h8 ? 1 : 0)] = k1;
+          const float k0 = v[0] + __shfl_xor_sync(0xffffffffu, v[2], 16);
+          const float k1 = v[1] + __shfl_xor_sync(0xffffffffu, v[3], 16);
+          float r = k0 + __shfl_xor_sync(0xffffffffu, k1, 8);
+          r += __shfl_xor_sync(0xffffffffu, r, 4);
+          if ((lane & 4) == 0) rdst[j * (8 * 16)] = r;
         }
         __syncwarp();
         if (lane == 0) {
