@@ -60,6 +60,47 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
   return make_float2(__uint_as_float((unsigned)aa), __uint_as_float((unsigned)(aa >> 32)));
 }
 
+// Two fp32 values in one 64-bit register pair, the operand form of the sm_100
+// f32x2 instructions; kept packed through hot loops so no repacking is needed.
+typedef unsigned long long f2x;
+__device__ __forceinline__ float2 f2x_unpack(f2x v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ f2x f2x_dup(float v) {
+  f2x r;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(r) : "f"(v));
+  return r;
+}
+__device__ __forceinline__ void f2x_fma(f2x& d, f2x a, f2x b) { asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(a), "l"(b)); }
+__device__ __forceinline__ f2x f2x_add(f2x a, f2x b) {
+  f2x r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// Warp-level tf32 tensor-core MMA (mma.sync m16n8k8, fp32 accumulate) and the
+// hi/lo split of an fp32 operand for the 3-pass product hi*hi + hi*lo + lo*hi
+// (about fp32 accuracy).  Fragment layout (g = lane / 4, t = lane % 4):
+// A: a0 = A[g][t], a1 = A[g+8][t], a2 = A[g][t+4], a3 = A[g+8][t+4];
+// B: b0 = B[t][g], b1 = B[t+4][g];  D: d0 = D[g][2t], d1 = D[g][2t+1],
+// d2 = D[g+8][2t], d3 = D[g+8][2t+1].
+__device__ __forceinline__ void mma_tf32_16x8x8(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// v = hi + lo with hi = v truncated to tf32 (sign, exponent and the top 10
+// mantissa bits: one logic op on the integer pipe rather than a conversion) and
+// lo = v - hi exactly; the MMA reads the top bits of lo, so hi*hi + hi*lo + lo*hi
+// misses about 2^-20 |a b| (the lo*lo term and lo's own truncation)
+__device__ __forceinline__ void split_tf32(float v, uint32_t& hi, uint32_t& lo) {
+  hi = __float_as_uint(v) & 0xFFFFE000u;
+  lo = __float_as_uint(v - __uint_as_float(hi));
+}
+
 inline unsigned grid_for(int64_t n, int block) {
   int64_t g = (n + block - 1) / block;
   return (unsigned)(g > 0 ? g : 1);

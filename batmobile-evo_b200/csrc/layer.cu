@@ -24,8 +24,18 @@ namespace bm {
 
 constexpr int kLT = 256;          // threads per layer CTA
 constexpr int kChunkC = 64;       // channels per pass (1024 rows of (c, m))
-constexpr int kRowPad = 66;       // smem stride of a (m2, a) row over channels (even: float2 reads)
-constexpr size_t kBsBytes = sizeof(float) * 256 * kRowPad;
+// Edge-summed tile in shared memory: 256 rows (m2 * 16 + m1) of 64 channels at
+// a pitch of 66 floats, rows stored in a permuted order that puts (m1 & 3,
+// (m2 >> 1) & 3) in the low four bits of the stored row.  The consumers' stores
+// of channel pairs (lanes = 4 m1 x 4 m2 pairs per phase) then hit 16 distinct
+// 8-byte bank pairs, and the contractors' loads (compile-time rows, lanes = 16
+// channel pairs per phase) stay free of conflicts with plain row offsets.
+constexpr int kTilePitch = 66;
+constexpr size_t kBsBytes = sizeof(float) * 256 * kTilePitch;
+__host__ __device__ constexpr int tile_row(int row) {
+  return (row & 3) | (((row >> 5) & 3) << 2) | (((row >> 2) & 3) << 4) | (((row >> 4) & 1) << 6) | (row & 128);
+}
+__host__ __device__ constexpr int tile_addr(int row, int c) { return tile_row(row) * kTilePitch + c; }
 
 __device__ __forceinline__ void cp_async16_zf(float* dst, const float* src, bool valid) {
   const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
@@ -45,7 +55,7 @@ __device__ __forceinline__ void contract_part(const float* __restrict__ Bs, int 
   float2 acc[R];
 #pragma unroll
   for (int i = 0; i < R; ++i) acc[i] = make_float2(0.0f, 0.0f);
-#define BM_X(j, row, c) ffma2(acc[j], make_float2((c), (c)), *reinterpret_cast<const float2*>(Bs + (row) * kRowPad + 2 * cp));
+#define BM_X(j, row, c) ffma2(acc[j], make_float2((c), (c)), *reinterpret_cast<const float2*>(Bs + tile_addr((row), 2 * cp)));
 #define BM_Y(j, g, i)                                                                   \
   {                                                                                     \
     constexpr int OFF_ = kGroupSlotOff[g], ROWS_ = (2 * (g) + 1) * kGroupPaths[g];     \
@@ -79,32 +89,50 @@ __device__ __forceinline__ void contract_part(const float* __restrict__ Bs, int 
 //                      and starts bulk copies of the sources' F rows (one
 //                      contiguous 4 KB row for 64 channels); lane 0 then arms
 //                      full[buf] with the batch's byte count;
-//   warps 0-7          (consumers) wait once per batch, then per edge: thread
-//                      t owns the (channel, m1) rows 4t .. 4t+3 and accumulates
-//                      their 16 m2 columns as packed pairs (fma.f32x2); the
-//                      batch is released (empty[buf]) once all of it is read.
-//                      At the end of an atom they write the tile into one of
-//                      two shared-memory tiles (bfull[tile]) and go on with
-//                      the next atom;
+//   warps 0-7          (consumers) wait once per batch; a batch of 8 edges is
+//                      one k-step of the atom's [1024 x 8] x [8 x 16] product
+//                      (rows (channel, m1), k = edge, columns m2) on the tensor
+//                      cores: warp w owns channels 8w .. 8w+7 as eight 16-row
+//                      m-tiles (two channels x 8 m1 each) and both 8-wide m2
+//                      tiles, and issues 3xTF32 mma.sync (hi*hi + hi*lo +
+//                      lo*hi, fp32 accumulators in registers); the batch is
+//                      released (empty[buf]) once its fragments are read.
+//                      At the end of an atom they store the accumulators as
+//                      channel pairs into one of two shared-memory tiles
+//                      (bfull[tile]) and go on with the next atom;
 //   warps 8-11         (contractors) contract each finished tile into slots
 //                      (balanced partition, two channels per thread) and
 //                      release it (bempty[tile]), overlapped with the
 //                      consumers' next atom.
 // kBatch divides 32 (the producers' edge groups).
+#ifndef BM_TGT_PAIR
+#define BM_TGT_PAIR 0
+#endif
 #ifndef BM_AGG_BATCH
 #define BM_AGG_BATCH 8
 #endif
 #ifndef BM_AGG_BUFS
 #define BM_AGG_BUFS 2
 #endif
+#ifdef BM_LDIAG
+static __device__ unsigned long long g_ldiag[16];
+#define LD_DECL unsigned long long ld[16] = {0}; unsigned long long lt0 = clock64(), lts = lt0;
+#define LD_ADD(slot) { unsigned long long _n = clock64(); ld[slot] += _n - lt0; lt0 = _n; }
+#define LD_MARK() lt0 = clock64();
+#define LD_FLUSH(tslot) if (MODE == 0 && lane == 0) { ld[tslot] = clock64() - lts; for (int _i = 0; _i < 16; ++_i) if (ld[_i]) atomicAdd(&g_ldiag[_i], ld[_i]); }
+#else
+#define LD_DECL
+#define LD_ADD(slot)
+#define LD_MARK()
+#define LD_FLUSH(tslot)
+#endif
 constexpr int kBatch = BM_AGG_BATCH;
 constexpr int kBufs = BM_AGG_BUFS;
 static_assert(32 % kBatch == 0, "batches must tile the producers' 32-edge groups");
-constexpr int kAggUnroll = 2;  // edges of a batch unrolled per consumer thread (1, 2, 4 measured alike; 8 slower)
 constexpr int kRing = kBatch * kBufs;
 constexpr int kProdWarps = 4;
 constexpr int kRowBytes = kChunkC * 16 * 4;           // F row of one channel chunk
-constexpr int kSlotBytes = kRowBytes + 16 * 4 + 16;   // row | Y_e | source index (+pad)
+constexpr int kSlotBytes = kRowBytes + 160;   // row | Y_e | source index | pad (slot pitch = 8 mod 32 words)
 constexpr int kContrWarps = 4;
 constexpr int kAggProdWarp0 = kLT / 32 + kContrWarps;
 constexpr size_t kAggSmem = (size_t)kRing * kSlotBytes + 2 * kBsBytes + 16;
@@ -160,7 +188,7 @@ layer_aggregate_kernel(const float* __restrict__ F, int CF, int CPF, const float
                        const float* __restrict__ escale, int* err) {
   extern __shared__ __align__(16) uint8_t agg_smem[];
   uint8_t* ring = agg_smem;
-  float* Bs2 = reinterpret_cast<float*>(agg_smem + (size_t)kRing * kSlotBytes);  // 2 x [256][kRowPad]
+  float* Bs2 = reinterpret_cast<float*>(agg_smem + (size_t)kRing * kSlotBytes);  // 2 x [256][kTilePitch]
   __shared__ uint64_t full[kBufs], empty[kBufs], bfull[2], bempty[2];
   __shared__ uint32_t turn;  // next batch allowed to take its buffer (stream order)
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
@@ -176,6 +204,11 @@ layer_aggregate_kernel(const float* __restrict__ F, int CF, int CPF, const float
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  // zero the ring once: the row of an invalid source is never copied and is
+  // multiplied by Y_e = 0, so it must hold finite values
+  for (int i = t; i < (int)(kRing * kSlotBytes / 16); i += blockDim.x)
+    reinterpret_cast<float4*>(ring)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  tc::fence_proxy_async_smem();
   __syncthreads();
   bool ok = true;
   const int chunks = (CF + kChunkC - 1) / kChunkC;
@@ -184,13 +217,16 @@ layer_aggregate_kernel(const float* __restrict__ F, int CF, int CPF, const float
     // ---------------------------------------------------------- contractors
     const int ct = t - kLT, cp = ct & 31, part = ct >> 5;
     uint32_t k = 0;
+    LD_DECL
     for (int64_t n = blockIdx.x; n < N && ok; n += gridDim.x) {
       for (int c0 = 0; c0 < CF && ok; c0 += kChunkC, ++k) {
         const uint32_t tile = k & 1;
+        LD_MARK()
         ok = tc::mbar_wait(&bfull[tile], (k >> 1) & 1, err);
         ok = __all_sync(0xffffffffu, ok);
+        LD_ADD(10)
         if (!ok) break;
-        const float* Bs = Bs2 + (size_t)tile * 256 * kRowPad;
+        const float* Bs = Bs2 + (size_t)tile * 256 * kTilePitch;
         if (c0 + 2 * cp < CPF) {  // padding channels (>= CF) accumulate zeros
           float* base = slots + c0 + 2 * cp;
           switch (part) {
@@ -201,13 +237,16 @@ layer_aggregate_kernel(const float* __restrict__ F, int CF, int CPF, const float
           }
         }
         __syncwarp();
+        LD_ADD(11)
         if (lane == 0) tc::mbar_arrive(&bempty[tile]);
       }
     }
+    LD_FLUSH(12)
   } else if (warp >= kAggProdWarp0) {
     // ----------------------------------------------------------- producers
     const int pw = warp - kAggProdWarp0;
     const int64_t step = gridDim.x;
+    LD_DECL
     // stream position of this warp's first atom: batches of the atoms before it
     uint32_t bi = 0;
     {
@@ -242,9 +281,12 @@ layer_aggregate_kernel(const float* __restrict__ F, int CF, int CPF, const float
             const uint32_t buf = bi % kBufs;
             // buffers are taken in stream order, so a buffer's empty barrier is
             // never more than one phase behind the batch waiting for it
+            LD_ADD(8)
             if (lane == 0) {
               ok = wait_turn(&turn, bi, err);
+              LD_ADD(5)
               if (ok && bi >= kBufs) ok = tc::mbar_wait(&empty[buf], ((bi / kBufs) - 1) & 1, err);
+              LD_ADD(6)
             }
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
@@ -253,7 +295,9 @@ layer_aggregate_kernel(const float* __restrict__ F, int CF, int CPF, const float
               uint8_t* sp = ring + (size_t)(buf * kBatch + (lane - b0)) * kSlotBytes;
               float4* yd = reinterpret_cast<float4*>(sp + kRowBytes);
 #pragma unroll
-              for (int b = 0; b < 4; ++b) yd[b] = make_float4(yv[4 * b], yv[4 * b + 1], yv[4 * b + 2], yv[4 * b + 3]);
+              for (int b = 0; b < 4; ++b)
+                yd[b] = o >= 0 ? make_float4(yv[4 * b], yv[4 * b + 1], yv[4 * b + 2], yv[4 * b + 3])
+                               : make_float4(0.f, 0.f, 0.f, 0.f);  // an invalid source adds nothing
               *reinterpret_cast<int64_t*>(sp + kRowBytes + 64) = o;
               if (o >= 0) tc::bulk_g2s(sp, F + (o * CF + c0) * 16, bytes, &full[buf]);
             }
@@ -265,6 +309,7 @@ layer_aggregate_kernel(const float* __restrict__ F, int CF, int CPF, const float
               tc::mbar_expect_tx(&full[buf], total);
               *reinterpret_cast<volatile uint32_t*>(&turn) = bi + 1;
             }
+            LD_ADD(7)
           }
         }
       }
@@ -273,71 +318,108 @@ layer_aggregate_kernel(const float* __restrict__ F, int CF, int CPF, const float
           (lane >= 1 && lane < kProdWarps) ? atom_batches(row_ptr, n + lane * step, N, chunks) : 0u;
       bi += __reduce_add_sync(0xffffffffu, nb);
     }
+    LD_FLUSH(9)
     // every started copy is consumed before the consumers finish, so nothing
     // is in flight once the CTA reaches its final barrier
   } else {
     // ------------------------------------------------------------ consumers
     uint32_t bi = 0, k = 0;
+    LD_DECL
     for (int64_t n = blockIdx.x; n < N && ok; n += gridDim.x) {
       const int64_t eb = row_ptr[n], ee = row_ptr[n + 1];
       for (int c0 = 0; c0 < CF && ok; c0 += kChunkC, ++k) {
-        float2 acc[4][8];
+        // one batch of 8 edges = one k-step of a [1024 x 8] x [8 x 16] product per
+        // atom: warp w owns channels 8 w .. 8 w + 7 (one 16-row m-tile each: the
+        // channel's 16 m1 rows), both 8-wide m2 n-tiles; 3xTF32 mma.sync
+        const int g = lane >> 2, tq = lane & 3;
+        const int cvalid = min(kChunkC, CF - c0);  // channels of this chunk
+        float acc[8][2][4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
+        for (int mt = 0; mt < 8; ++mt)
 #pragma unroll
-          for (int b = 0; b < 8; ++b) acc[q][b] = make_float2(0.0f, 0.0f);
-        const bool rv = 4 * t < min(kChunkC, CF - c0) * 16;
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[mt][nt][i] = 0.0f;
         for (int64_t e0 = eb; e0 < ee; e0 += kBatch, ++bi) {
           const int cnt = (int)imin64(kBatch, ee - e0);
           const uint32_t buf = bi % kBufs;
+          LD_MARK()
           if (!tc::mbar_wait(&full[buf], (bi / kBufs) & 1, err)) { ok = false; break; }
-          const uint8_t* bp = ring + (size_t)buf * kBatch * kSlotBytes;
-#pragma unroll kAggUnroll
-          for (int j = 0; j < cnt; ++j) {
-            const uint8_t* sp = bp + (size_t)j * kSlotBytes;
-            const int64_t o = *reinterpret_cast<const int64_t*>(sp + kRowBytes + 64);
-            const float4 xr = reinterpret_cast<const float4*>(sp)[t];
-            float2 yv[8];
+          LD_ADD(0)
+          const float* s0 = reinterpret_cast<const float*>(ring + (size_t)(buf * kBatch + tq) * kSlotBytes);
+          const float* s1 = reinterpret_cast<const float*>(ring + (size_t)(buf * kBatch + tq + 4) * kSlotBytes);
+          // B = Y (k = edge slot, n = m2); slots past the batch add nothing
+          uint32_t bh[2][2], bl[2][2];
 #pragma unroll
-            for (int b = 0; b < 8; b += 2) {
-              const float4 y4 = reinterpret_cast<const float4*>(sp + kRowBytes)[b >> 1];
-              yv[b] = make_float2(y4.x, y4.y);
-              yv[b + 1] = make_float2(y4.z, y4.w);
-            }
-            const float4 xv = (o >= 0 && rv) ? xr : make_float4(0.f, 0.f, 0.f, 0.f);
-            const float2 x0 = make_float2(xv.x, xv.x), x1 = make_float2(xv.y, xv.y);
-            const float2 x2 = make_float2(xv.z, xv.z), x3 = make_float2(xv.w, xv.w);
+          for (int nt = 0; nt < 2; ++nt) {
+            split_tf32(tq < cnt ? s0[kChunkC * 16 + 8 * nt + g] : 0.0f, bh[nt][0], bl[nt][0]);
+            split_tf32(tq + 4 < cnt ? s1[kChunkC * 16 + 8 * nt + g] : 0.0f, bh[nt][1], bl[nt][1]);
+          }
+          // m-tile mt: rows 0-7 = channel c, rows 8-15 = channel c + 1 (c = 8 w +
+          // 2 (mt / 2)), both at m1 = 8 (mt % 2) + row % 8.  All A loads come first
+          // (no branches between them and the MMAs); channels past the chunk's
+          // last one read as zeros
+          float xr[8][4];
+          const bool fullw = 8 * warp + 8 <= cvalid;
 #pragma unroll
-            for (int b = 0; b < 8; ++b) {
-              ffma2(acc[0][b], x0, yv[b]);
-              ffma2(acc[1][b], x1, yv[b]);
-              ffma2(acc[2][b], x2, yv[b]);
-              ffma2(acc[3][b], x3, yv[b]);
-            }
+          for (int mt = 0; mt < 8; ++mt) {
+            const int cc = 8 * warp + 2 * (mt >> 1);
+            const int o = 16 * cc + 8 * (mt & 1) + g;
+            const bool v0 = fullw || cc < cvalid, v1 = fullw || cc + 1 < cvalid;
+            xr[mt][0] = v0 ? s0[o] : 0.0f;
+            xr[mt][1] = v1 ? s0[o + 16] : 0.0f;
+            xr[mt][2] = v0 ? s1[o] : 0.0f;
+            xr[mt][3] = v1 ? s1[o + 16] : 0.0f;
+          }
+          // m-tiles in pairs, the three terms outermost: four independent
+          // accumulators between dependent MMAs
+#pragma unroll
+          for (int mp = 0; mp < 8; mp += 2) {
+            uint32_t ah[2][4], al[2][4];
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+              for (int i = 0; i < 4; ++i) split_tf32(xr[mp + h][i], ah[h][i], al[h][i]);
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+              for (int nt = 0; nt < 2; ++nt) mma_tf32_16x8x8(acc[mp + h][nt], al[h], bh[nt][0], bh[nt][1]);
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+              for (int nt = 0; nt < 2; ++nt) mma_tf32_16x8x8(acc[mp + h][nt], ah[h], bl[nt][0], bl[nt][1]);
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+              for (int nt = 0; nt < 2; ++nt) mma_tf32_16x8x8(acc[mp + h][nt], ah[h], bh[nt][0], bh[nt][1]);
           }
           __syncwarp();
+          LD_ADD(1)
           if (lane == 0) tc::mbar_arrive(&empty[buf]);
         }
         // hand the tile to the contractors (the tile two atoms back is free once they are done with it)
         const uint32_t tile = k & 1;
+        LD_MARK()
         if (ok && k >= 2) ok = tc::mbar_wait(&bempty[tile], ((k - 2) >> 1) & 1, err);
+        LD_ADD(2)
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
-        float* Bs = Bs2 + (size_t)tile * 256 * kRowPad;
+        float* Bs = Bs2 + (size_t)tile * 256 * kTilePitch;
+        // tile row (m2 * 16 + m1), column = channel
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int r = 4 * t + q;
-          const int cl = r >> 4, a = r & 15;
+        for (int mt = 0; mt < 8; ++mt)
 #pragma unroll
-          for (int b = 0; b < 8; ++b) {
-            Bs[((2 * b) * 16 + a) * kRowPad + cl] = acc[q][b].x;
-            Bs[((2 * b + 1) * 16 + a) * kRowPad + cl] = acc[q][b].y;
+          for (int nt = 0; nt < 2; ++nt) {
+            const int c = 8 * warp + 2 * (mt >> 1), m1 = 8 * (mt & 1) + g, m2 = 8 * nt + 2 * tq;
+            *reinterpret_cast<float2*>(Bs + tile_addr(m2 * 16 + m1, c)) = make_float2(acc[mt][nt][0], acc[mt][nt][2]);
+            *reinterpret_cast<float2*>(Bs + tile_addr((m2 + 1) * 16 + m1, c)) = make_float2(acc[mt][nt][1], acc[mt][nt][3]);
           }
-        }
         __syncwarp();
+        LD_ADD(3)
         if (lane == 0) tc::mbar_arrive(&bfull[tile]);
       }
     }
+    LD_FLUSH(4)
   }
   __syncthreads();
 }
@@ -870,7 +952,12 @@ layer_target_ws_kernel(const __grid_constant__ CUtensorMap xmap, const float* __
     const int qq = lane & 3, ce = 8 * warp + (lane >> 2);
     const int sw = (ce >> 1) & 3;  // 64-byte swizzle of channel row ce
     const bool hi16 = lane & 16, h8 = lane & 8;
-    const int red_m2 = 4 * qq + (hi16 ? 2 : 0) + (h8 ? 1 : 0);  // m2 this lane's reduced value belongs to
+#if BM_TGT_PAIR
+    const bool pm_hi = h8, pm_lo = lane & 4;  // reduce-scatter stages over lane bits 16 (edge), 8, 4 (m2)
+#else
+    const bool pm_hi = hi16, pm_lo = h8;      // stages over lane bits 16, 8 (m2), then a sum over bit 4
+#endif
+    const int red_m2 = 4 * qq + (pm_hi ? 2 : 0) + (pm_lo ? 1 : 0);  // m2 of this lane's reduced value
     uint32_t bi = 0, ac = 0;
     bool stuck = false;  // a bounded wait of this warp gave up in the edge loop (warp-uniform)
     for (int64_t n = blockIdx.x; n < N && ok; n += gridDim.x) {
@@ -894,19 +981,19 @@ layer_target_ws_kernel(const __grid_constant__ CUtensorMap xmap, const float* __
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&dempty);
       consumer_sync();
-      // d2[p][j] = (dB[ce, 2p, m], dB[ce, 2p+1, m]) with m = 4 qq + (j ^ xo): the lane's
-      // m2 order is permuted by its reduce-scatter position, so that every lane
-      // keeps local {0, 1} and sends {2, 3} at the first shuffle stage and keeps
-      // 0, sends 1 at the second (no lane-dependent selects in the edge loop)
-      float2 d2[8][4];
+      // d2[p][j] = (dB[ce, 2p, m], dB[ce, 2p+1, m]) with m = 4 qq + (j ^ pm): the lane's
+      // m2 order is permuted by its reduce-scatter position (pm), so that at each
+      // shuffle stage every lane keeps its low local values and sends the high ones
+      // (no lane-dependent selects in the edge loop)
+      f2x d2[8][4];
 #pragma unroll
       for (int p = 0; p < 8; ++p) {
-        const float4 lo = *dbt_chunk(tile, ce, qq, 2 * p + (hi16 ? 1 : 0));  // local j = 0, 1
-        const float4 up = *dbt_chunk(tile, ce, qq, 2 * p + (hi16 ? 0 : 1));  // local j = 2, 3
-        d2[p][0] = h8 ? make_float2(lo.z, lo.w) : make_float2(lo.x, lo.y);
-        d2[p][1] = h8 ? make_float2(lo.x, lo.y) : make_float2(lo.z, lo.w);
-        d2[p][2] = h8 ? make_float2(up.z, up.w) : make_float2(up.x, up.y);
-        d2[p][3] = h8 ? make_float2(up.x, up.y) : make_float2(up.z, up.w);
+        const ulonglong2 lo = *reinterpret_cast<const ulonglong2*>(dbt_chunk(tile, ce, qq, 2 * p + (pm_hi ? 1 : 0)));
+        const ulonglong2 up = *reinterpret_cast<const ulonglong2*>(dbt_chunk(tile, ce, qq, 2 * p + (pm_hi ? 0 : 1)));
+        d2[p][0] = pm_lo ? lo.y : lo.x;
+        d2[p][1] = pm_lo ? lo.x : lo.y;
+        d2[p][2] = pm_lo ? up.y : up.x;
+        d2[p][3] = pm_lo ? up.x : up.y;
       }
       for (int64_t e0 = eb; e0 < ee && !stuck; e0 += kBatch, ++bi) {
         const int cnt = (int)imin64(kBatch, ee - e0);
@@ -918,32 +1005,70 @@ layer_target_ws_kernel(const __grid_constant__ CUtensorMap xmap, const float* __
           stuck = true;
           break;
         }
+        // rows of invalid sources and channels >= C_in hold finite data (the ring
+        // starts zeroed); the epilogue drops invalid edges, dB is zero past C_in
         const uint8_t* row0 = ring + (size_t)(buf * kBatch) * kTRowBytes + ce * 64;
-        float* rdst = &red[par][0][warp][red_m2];
-#pragma unroll 2
-        for (int j = 0; j < cnt; ++j) {
-          // rows of invalid sources and channels >= C_in hold finite data (the ring
-          // starts zeroed); the epilogue drops invalid edges, dB is zero past C_in
-          const uint8_t* row = row0 + (size_t)j * kTRowBytes;
-          float2 a[2][4];
+#if BM_TGT_PAIR
+        // two edges per step: lanes with bit 16 set take them in the other order,
+        // so the 8 partials reduce-scatter to one (edge, m2) value per lane
+        for (int j = 0; j < cnt; j += 2) {
+          const ulonglong2* ra = reinterpret_cast<const ulonglong2*>(row0 + (size_t)(j + (hi16 ? 1 : 0)) * kTRowBytes);
+          const ulonglong2* rb = reinterpret_cast<const ulonglong2*>(row0 + (size_t)(j + (hi16 ? 0 : 1)) * kTRowBytes);
+          f2x a[2][4], b[2][4];
 #pragma unroll
           for (int h = 0; h < 2; ++h)
 #pragma unroll
-            for (int m = 0; m < 4; ++m) a[h][m] = make_float2(0.f, 0.f);
+            for (int m = 0; m < 4; ++m) a[h][m] = b[h][m] = 0ull;
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const float4 x4 = *reinterpret_cast<const float4*>(row + ((i ^ sw) << 4));
-            const float2 xa = make_float2(x4.x, x4.y), xb = make_float2(x4.z, x4.w);
+            const ulonglong2 xa = ra[i ^ sw], xb = rb[i ^ sw];
 #pragma unroll
             for (int m = 0; m < 4; ++m) {
-              ffma2(a[i >> 1][m], xa, d2[2 * i][m]);
-              ffma2(a[i >> 1][m], xb, d2[2 * i + 1][m]);
+              f2x_fma(a[i >> 1][m], xa.x, d2[2 * i][m]);
+              f2x_fma(b[i >> 1][m], xb.x, d2[2 * i][m]);
+              f2x_fma(a[i >> 1][m], xa.y, d2[2 * i + 1][m]);
+              f2x_fma(b[i >> 1][m], xb.y, d2[2 * i + 1][m]);
+            }
+          }
+          float va[4], vb[4];
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {
+            const float2 sa = f2x_unpack(f2x_add(a[0][m], a[1][m]));
+            const float2 sb = f2x_unpack(f2x_add(b[0][m], b[1][m]));
+            va[m] = sa.x + sa.y;
+            vb[m] = sb.x + sb.y;
+          }
+          float k[4];
+#pragma unroll
+          for (int m = 0; m < 4; ++m) k[m] = va[m] + __shfl_xor_sync(0xffffffffu, vb[m], 16);
+          const float k0 = k[0] + __shfl_xor_sync(0xffffffffu, k[2], 8);
+          const float k1 = k[1] + __shfl_xor_sync(0xffffffffu, k[3], 8);
+          const float r = k0 + __shfl_xor_sync(0xffffffffu, k1, 4);
+          const int je = j + (hi16 ? 1 : 0);
+          if (je < cnt) red[par][je][warp][red_m2] = r;
+        }
+#else
+#pragma unroll 2
+        for (int j = 0; j < cnt; ++j) {
+          const ulonglong2* row = reinterpret_cast<const ulonglong2*>(row0 + (size_t)j * kTRowBytes);
+          f2x a[2][4];
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int m = 0; m < 4; ++m) a[h][m] = 0ull;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const ulonglong2 x2 = row[i ^ sw];
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+              f2x_fma(a[i >> 1][m], x2.x, d2[2 * i][m]);
+              f2x_fma(a[i >> 1][m], x2.y, d2[2 * i + 1][m]);
             }
           }
           float v[4];
 #pragma unroll
           for (int m = 0; m < 4; ++m) {
-            const float2 s2 = fadd2(a[0][m], a[1][m]);
+            const float2 s2 = f2x_unpack(f2x_add(a[0][m], a[1][m]));
             v[m] = s2.x + s2.y;
           }
           // reduce-scatter over the warp's 8 channels (lanes with equal qq)
@@ -951,8 +1076,9 @@ layer_target_ws_kernel(const __grid_constant__ CUtensorMap xmap, const float* __
           const float k1 = v[1] + __shfl_xor_sync(0xffffffffu, v[3], 16);
           float r = k0 + __shfl_xor_sync(0xffffffffu, k1, 8);
           r += __shfl_xor_sync(0xffffffffu, r, 4);
-          if ((lane & 4) == 0) rdst[j * (8 * 16)] = r;
+          if ((lane & 4) == 0) red[par][j][warp][red_m2] = r;
         }
+#endif
         __syncwarp();
         if (lane == 0) {
           tc::mbar_arrive(&empty[buf]);
@@ -1131,6 +1257,15 @@ int bm_layer_bwd_targets(const float* x, const float* v, const float* W, const i
 
 }  // extern "C"
 
+#ifdef BM_LDIAG
+extern "C" __attribute__((visibility("default"))) int bm_ldiag_read(unsigned long long* out) {
+  cudaDeviceSynchronize();
+  cudaMemcpyFromSymbol(out, bm::g_ldiag, sizeof(unsigned long long) * 16);
+  unsigned long long z[16] = {0};
+  cudaMemcpyToSymbol(bm::g_ldiag, z, sizeof(z));
+  return 0;
+}
+#endif
 #ifdef BM_DIAG
 extern "C" __attribute__((visibility("default"))) int bm_gdiag_read(unsigned long long* out) {
   cudaDeviceSynchronize();
