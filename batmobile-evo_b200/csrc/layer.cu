@@ -108,6 +108,9 @@ __device__ __forceinline__ void contract_part(const float* __restrict__ Bs, int 
 #ifndef BM_TGT_PAIR
 #define BM_TGT_PAIR 0
 #endif
+#ifndef BM_AGG_MQ
+#define BM_AGG_MQ 4
+#endif
 #ifndef BM_AGG_BATCH
 #define BM_AGG_BATCH 8
 #endif
@@ -371,25 +374,25 @@ layer_aggregate_kernel(const float* __restrict__ F, int CF, int CPF, const float
             xr[mt][2] = v0 ? s1[o] : 0.0f;
             xr[mt][3] = v1 ? s1[o + 16] : 0.0f;
           }
-          // m-tiles in pairs, the three terms outermost: four independent
-          // accumulators between dependent MMAs
+          // m-tiles in groups of BM_AGG_MQ, the three terms outermost: 2 BM_AGG_MQ
+          // independent accumulators between dependent MMAs (mma.sync latency)
 #pragma unroll
-          for (int mp = 0; mp < 8; mp += 2) {
-            uint32_t ah[2][4], al[2][4];
+          for (int mp = 0; mp < 8; mp += BM_AGG_MQ) {
+            uint32_t ah[BM_AGG_MQ][4], al[BM_AGG_MQ][4];
 #pragma unroll
-            for (int h = 0; h < 2; ++h)
+            for (int h = 0; h < BM_AGG_MQ; ++h)
 #pragma unroll
               for (int i = 0; i < 4; ++i) split_tf32(xr[mp + h][i], ah[h][i], al[h][i]);
 #pragma unroll
-            for (int h = 0; h < 2; ++h)
+            for (int h = 0; h < BM_AGG_MQ; ++h)
 #pragma unroll
               for (int nt = 0; nt < 2; ++nt) mma_tf32_16x8x8(acc[mp + h][nt], al[h], bh[nt][0], bh[nt][1]);
 #pragma unroll
-            for (int h = 0; h < 2; ++h)
+            for (int h = 0; h < BM_AGG_MQ; ++h)
 #pragma unroll
               for (int nt = 0; nt < 2; ++nt) mma_tf32_16x8x8(acc[mp + h][nt], ah[h], bl[nt][0], bl[nt][1]);
 #pragma unroll
-            for (int h = 0; h < 2; ++h)
+            for (int h = 0; h < BM_AGG_MQ; ++h)
 #pragma unroll
               for (int nt = 0; nt < 2; ++nt) mma_tf32_16x8x8(acc[mp + h][nt], ah[h], bh[nt][0], bh[nt][1]);
           }
@@ -1090,6 +1093,327 @@ layer_target_ws_kernel(const __grid_constant__ CUtensorMap xmap, const float* __
   __syncthreads();
 }
 
+// ---------------------------------------------------------------------------
+// Target-side backward on warp-level tensor cores (C_in <= 64).  Per target
+// atom n the edge gradient is a product with K = 1024 rows (channel, m1):
+//   dY^T[m2, e] = sum_K dB_n^T[m2, K] x[src e]^T[K, e],  dB_n = CG^T dS_n,
+// i.e. per batch of 8 edges an [16 x 1024] x [1024 x 8] product (mma.sync
+// m16n8k8 tf32, M = m2, N = edges, 3xTF32: hi*hi + hi*lo + lo*hi).
+// Persistent CTAs (one per SM) walk the atoms n_k = blockIdx.x + k * gridDim.x:
+//   warps 16-18 (producers)  as in the SIMT kernel: per atom the dS block by
+//                            bulk copies, then its edges in batches of kBatch
+//                            (metadata + the source's x row, one bulk copy of
+//                            C_in x 64 bytes into a slot padded to 4 mod 32
+//                            words, so a fragment load of 8 edges x 4 K hits 32
+//                            banks);
+//   warps 0-15 (consumers)   per atom warps 0-7 build dB = CG^T dS (warp w: m2
+//                            quarter w % 4 for 32 channels) into a [m2][K]
+//                            tile; every warp w then keeps the A fragments of its
+//                            K slice 64 w .. 64 w + 63 (channels 4w .. 4w+3) in
+//                            registers, split into tf32 hi/lo (64 registers);
+//                            per batch: 8 k-steps of 3 MMAs on the x fragments
+//                            (two loads per k-step), the warp's partial
+//                            dY^T[16 x 8] into shared memory;
+//   warp 19 (epilogue)       per batch: adds the 16 K-slice partials and applies
+//                            the SH and normalisation chain rule -> dv_e.
+// ---------------------------------------------------------------------------
+constexpr int kTMCons = 16;                                  // consumer warps (K slices of 64)
+constexpr int kTMProd = 3;                                   // producer warps
+constexpr int kTMEpi = kTMCons + kTMProd;                    // epilogue warp
+constexpr int kTMThreads = 32 * (kTMCons + kTMProd + 1);
+constexpr int kTMSlot = 4096 + 16;                           // x row slot (bytes): 4 mod 32 words
+constexpr int kTMdBPitch = 1028;                             // dB tile [m2][K] row pitch (floats)
+constexpr int kTMRedPitch = 20;                              // partials [warp][edge][m2 (+pad)]
+constexpr size_t kTMRingBytes = (size_t)kTBufs * kBatch * kTMSlot;
+constexpr size_t kTMdBBytes = (size_t)16 * kTMdBPitch * 4;
+constexpr size_t kTMRedBytes = (size_t)2 * kTMCons * kBatch * kTMRedPitch * 4;
+constexpr size_t kTMSmem = kTMRingBytes + kTdSBytes + kTMdBBytes + kTMRedBytes + 16;
+static_assert(kBatch == 8, "one batch is one 8-wide n-tile of edges");
+
+__device__ __forceinline__ void cons16_sync() { asm volatile("bar.sync 1, %0;" ::"n"(32 * kTMCons) : "memory"); }
+__device__ __forceinline__ bool cons16_sync_or(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.or.pred p, 1, %2, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "n"(32 * kTMCons)
+      : "memory");
+  return r != 0;
+}
+
+// dB tile element (m2, c, m1): row m2 of 1028 floats, channel c at 16 c, the
+// four 16-byte m1 chunks of a channel XOR-swizzled by (c >> 1) & 3 (the
+// builder's 8-channel phases and the fragment loads are conflict-free).
+__device__ __forceinline__ int dbk_off(int m2, int c, int m1) {
+  return m2 * kTMdBPitch + c * 16 + 4 * ((m1 >> 2) ^ ((c >> 1) & 3)) + (m1 & 3);
+}
+
+// Builds dB for m2 quarter Q (warp-uniform, lane = channel c) into the [m2][K] tile.
+template <int Q>
+__device__ __forceinline__ void target_build_dBk(const float* dSs, float* dBt, int c, bool cv) {
+  float2 d[16][2];  // [m1][m2 pair within the quarter]
+#pragma unroll
+  for (int i = 0; i < 16; ++i) d[i][0] = d[i][1] = make_float2(0.0f, 0.0f);
+  if (cv) dB_quarter<Q>(dSs, c, d);
+#pragma unroll
+  for (int m = 0; m < 4; ++m)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = (m & 1) ? d[4 * j + u][m >> 1].y : d[4 * j + u][m >> 1].x;
+      *reinterpret_cast<float4*>(dBt + dbk_off(4 * Q + m, c, 4 * j)) = make_float4(v[0], v[1], v[2], v[3]);
+    }
+}
+
+__global__ void __launch_bounds__(kTMThreads, 1)
+layer_target_mma_kernel(const float* __restrict__ x, const float* __restrict__ dS, int Ci, int CPi,
+                        const float* __restrict__ vec, const int64_t* __restrict__ src,
+                        const int64_t* __restrict__ row_ptr, const int64_t* __restrict__ perm,
+                        float* __restrict__ gv, int64_t N, int64_t NX, const float* __restrict__ escale,
+                        float* __restrict__ gscale, int* err) {
+  extern __shared__ __align__(16) uint8_t tm_smem[];
+  uint8_t* ring = tm_smem;                                                   // [kTBufs * kBatch][kTMSlot]
+  float* dSs = reinterpret_cast<float*>(tm_smem + kTMRingBytes);            // [156][64]
+  float* dBt = reinterpret_cast<float*>(tm_smem + kTMRingBytes + kTdSBytes);  // [16][kTMdBPitch]
+  float* red = reinterpret_cast<float*>(tm_smem + kTMRingBytes + kTdSBytes + kTMdBBytes);  // [2][16][8][20]
+  __shared__ TMeta meta[kTBufs * kBatch];
+  __shared__ uint64_t full[kTBufs], empty[kTBufs], dfull, dempty, red_full[2], red_empty[2];
+  __shared__ uint32_t turn;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  if (t == 0) {
+    turn = 0;
+    for (int i = 0; i < kTBufs; ++i) {
+      tc::mbar_init(&full[i], 1);
+      tc::mbar_init(&empty[i], kTMCons + 1);  // consumers + epilogue
+    }
+    tc::mbar_init(&dfull, 1);
+    tc::mbar_init(&dempty, 8);  // the eight builder warps
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&red_full[i], kTMCons);
+      tc::mbar_init(&red_empty[i], 1);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  // zero the x ring once: bytes past C_in x 64 of a slot are never written, and
+  // the fragment loads read all 64 channels (dB is zero there)
+  for (int i = t; i < (int)(kTMRingBytes / 16); i += blockDim.x)
+    reinterpret_cast<float4*>(ring)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  tc::fence_proxy_async_smem();
+  __syncthreads();
+  bool ok = true;
+  const uint32_t row_bytes = (uint32_t)Ci * 64u;
+
+  if (warp >= kTMCons && warp < kTMEpi) {
+    // ----------------------------------------------------------- producers
+    const int pw = warp - kTMCons;
+    const int64_t step = gridDim.x;
+    uint32_t bi = 0, ac = 0;
+    {
+      uint32_t nb, na;
+      target_atom_counts(row_ptr, blockIdx.x + lane * step, N, nb, na);
+      if (lane >= pw) nb = na = 0;
+      bi = __reduce_add_sync(0xffffffffu, nb);
+      ac = __reduce_add_sync(0xffffffffu, na);
+    }
+    for (int64_t n = blockIdx.x + pw * step; n < N && ok; n += kTMProd * step) {
+      const int64_t eb = row_ptr[n], ee = row_ptr[n + 1];
+      if (ee > eb) {
+        if (lane == 0) {
+          ok = wait_turn(&turn, bi, err);
+          if (ok && ac >= 1) ok = tc::mbar_wait(&dempty, (ac - 1) & 1, err);
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (ok) {
+          if (CPi == 64) {
+            if (lane < 4) {
+              const int g = lane;
+              const uint32_t rows = (uint32_t)((2 * g + 1) * group_paths(g));
+              tc::bulk_g2s(dSs + (size_t)group_slot_off(g) * 64,
+                           dS + N * 64 * (int64_t)group_slot_off(g) + n * (int64_t)rows * 64, rows * 256u, &dfull);
+            }
+          } else {
+            for (int sl = lane; sl < kSlots; sl += 32) {
+              int g = 0;
+              while (g < 3 && sl >= group_slot_off(g + 1)) ++g;
+              const int local = sl - group_slot_off(g);
+              const int64_t rows = (2 * g + 1) * group_paths(g);
+              tc::bulk_g2s(dSs + (size_t)sl * 64, dS + N * CPi * (int64_t)group_slot_off(g) + (n * rows + local) * CPi,
+                           (uint32_t)CPi * 4u, &dfull);
+            }
+          }
+          __syncwarp();
+          if (lane == 0) tc::mbar_expect_tx(&dfull, (uint32_t)kSlots * (uint32_t)CPi * 4u);
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        ++ac;
+        for (int64_t g0 = eb; g0 < ee && ok; g0 += 32) {
+          const int gcnt = (int)imin64(32, ee - g0);
+          TMeta m{};
+          int64_t srow = -1;
+          if (lane < gcnt) {
+            const int64_t e = perm ? perm[g0 + lane] : g0 + lane;
+            const int64_t sidx = src[e];
+            srow = (sidx >= 0 && sidx < NX) ? sidx : -1;
+            m.e = e;
+            m.vx = vec[3 * e];
+            m.vy = vec[3 * e + 1];
+            m.vz = vec[3 * e + 2];
+            m.valid = srow >= 0 ? 1 : 0;
+            m.sc = escale ? escale[e] : 1.0f;
+          }
+          for (int b0 = 0; b0 < gcnt && ok; b0 += kBatch, ++bi) {
+            const int cnt = min(kBatch, gcnt - b0);
+            const bool act = lane >= b0 && lane < b0 + cnt;
+            const uint32_t buf = bi % kTBufs;
+            if (lane == 0) {
+              if (b0 > 0 || g0 > eb) ok = wait_turn(&turn, bi, err);  // the first batch holds the turn already
+              if (ok && bi >= kTBufs) ok = tc::mbar_wait(&empty[buf], ((bi / kTBufs) - 1) & 1, err);
+            }
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            const uint32_t mine = (act && srow >= 0) ? row_bytes : 0u;
+            if (act) {
+              const int sl = buf * kBatch + (lane - b0);
+              meta[sl] = m;
+              if (srow >= 0) tc::bulk_g2s(ring + (size_t)sl * kTMSlot, x + srow * (int64_t)Ci * 16, row_bytes, &full[buf]);
+            }
+            const uint32_t total = __reduce_add_sync(0xffffffffu, mine);
+            __syncwarp();
+            if (lane == 0) {
+              tc::mbar_expect_tx(&full[buf], total);
+              *reinterpret_cast<volatile uint32_t*>(&turn) = bi + 1;
+            }
+          }
+        }
+      }
+      uint32_t nb = 0, na = 0;
+      if (lane >= 1 && lane < kTMProd) target_atom_counts(row_ptr, n + lane * step, N, nb, na);
+      bi += __reduce_add_sync(0xffffffffu, nb);
+      ac += __reduce_add_sync(0xffffffffu, na);
+    }
+  } else if (warp == kTMEpi) {
+    // ------------------------------------------------------------ epilogue
+    // per batch: dY_e = sum of the 16 K-slice partials, then the SH and
+    // normalisation chain rule -> dv_e; lane = (edge lane / 4, m2 quarter lane % 4)
+    const int je = lane >> 2, mq = lane & 3;
+    uint32_t bi = 0;
+    for (int64_t n = blockIdx.x; n < N && ok; n += gridDim.x) {
+      const int64_t eb = row_ptr[n], ee = row_ptr[n + 1];
+      for (int64_t e0 = eb; e0 < ee && ok; e0 += kBatch, ++bi) {
+        const int cnt = (int)imin64(kBatch, ee - e0);
+        const uint32_t buf = bi % kTBufs, par = bi & 1;
+        if (!tc::mbar_wait(&red_full[par], (bi >> 1) & 1, err)) { ok = false; break; }
+        const float* rp = red + (size_t)par * kTMCons * kBatch * kTMRedPitch + je * kTMRedPitch + 4 * mq;
+        float4 dq = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int w = 0; w < kTMCons; ++w) {
+          const float4 r4 = *reinterpret_cast<const float4*>(rp + w * kBatch * kTMRedPitch);
+          dq.x += r4.x; dq.y += r4.y; dq.z += r4.z; dq.w += r4.w;
+        }
+        float dyv[16];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int srcl = (lane & ~3) + k;
+          dyv[4 * k] = __shfl_sync(0xffffffffu, dq.x, srcl);
+          dyv[4 * k + 1] = __shfl_sync(0xffffffffu, dq.y, srcl);
+          dyv[4 * k + 2] = __shfl_sync(0xffffffffu, dq.z, srcl);
+          dyv[4 * k + 3] = __shfl_sync(0xffffffffu, dq.w, srcl);
+        }
+        if (mq == 0 && je < cnt) {
+          const TMeta mm = meta[buf * kBatch + je];
+          if (!mm.valid) {  // the ring slot of an invalid source holds stale rows
+#pragma unroll
+            for (int m2 = 0; m2 < 16; ++m2) dyv[m2] = 0.0f;
+          }
+          target_edge_epilogue(mm.e, mm.vx, mm.vy, mm.vz, mm.sc, dyv, gv, gscale);
+        }
+        __syncwarp();
+        if (lane == 0) {
+          tc::mbar_arrive(&red_empty[par]);
+          tc::mbar_arrive(&empty[buf]);
+        }
+      }
+    }
+  } else {
+    // ----------------------------------------------------------- consumers
+    const int g = lane >> 2, tq = lane & 3;
+    uint32_t bi = 0, ac = 0;
+    bool stuck = false;  // a bounded wait of this warp gave up in the edge loop (warp-uniform)
+    for (int64_t n = blockIdx.x; n < N && ok; n += gridDim.x) {
+      const int64_t eb = row_ptr[n], ee = row_ptr[n + 1];
+      if (ee <= eb) continue;
+      const bool gave_up = stuck || !__all_sync(0xffffffffu, warp >= 8 || tc::mbar_wait(&dfull, ac & 1, err));
+      ++ac;
+      // every warp is done with the previous atom's tile; if any consumer gave
+      // up on a wait, all consumer warps leave here together
+      if (cons16_sync_or(gave_up)) { ok = false; break; }
+      if (warp < 8) {
+        const int cb = (warp >> 2) * 32 + lane;
+        const bool cbv = cb < Ci;
+        switch (warp & 3) {
+          case 0: target_build_dBk<0>(dSs, dBt, cb, cbv); break;
+          case 1: target_build_dBk<1>(dSs, dBt, cb, cbv); break;
+          case 2: target_build_dBk<2>(dSs, dBt, cb, cbv); break;
+          default: target_build_dBk<3>(dSs, dBt, cb, cbv); break;
+        }
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&dempty);
+      }
+      cons16_sync();
+      // A fragments of this warp's K slice: k-step s covers channel 4 w + s / 2,
+      // m1 = 8 (s % 2) + 0..7; a0 = dB^T[g][t], a1 = [g+8][t], a2 = [g][t+4], a3 = [g+8][t+4]
+      uint32_t ah[8][4], al[8][4];
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        const int c = 4 * warp + (s >> 1), m1 = 8 * (s & 1) + tq;
+        split_tf32(dBt[dbk_off(g, c, m1)], ah[s][0], al[s][0]);
+        split_tf32(dBt[dbk_off(g + 8, c, m1)], ah[s][1], al[s][1]);
+        split_tf32(dBt[dbk_off(g, c, m1 + 4)], ah[s][2], al[s][2]);
+        split_tf32(dBt[dbk_off(g + 8, c, m1 + 4)], ah[s][3], al[s][3]);
+      }
+      for (int64_t e0 = eb; e0 < ee && !stuck; e0 += kBatch, ++bi) {
+        const uint32_t buf = bi % kTBufs, par = bi & 1;
+        // warp votes: the warp stays converged and meets the others at the next cons16_sync_or
+        if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[buf], (bi / kTBufs) & 1, err))) { stuck = true; break; }
+        // red[par] is free once the epilogue has finished the batch two back
+        if (bi >= 2 && !__all_sync(0xffffffffu, tc::mbar_wait(&red_empty[par], ((bi >> 1) - 1) & 1, err))) {
+          stuck = true;
+          break;
+        }
+        // B fragments: b0 = x[src of slot g][K0 + t], b1 = [K0 + t + 4]; slots past
+        // the batch hold finite stale rows whose results the epilogue drops
+        const float* xs = reinterpret_cast<const float*>(ring + (size_t)(buf * kBatch + g) * kTMSlot) + 64 * warp + tq;
+        float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+          uint32_t bh0, bl0, bh1, bl1;
+          split_tf32(xs[8 * s], bh0, bl0);
+          split_tf32(xs[8 * s + 4], bh1, bl1);
+          mma_tf32_16x8x8(acc[s & 1], al[s], bh0, bh1);
+          mma_tf32_16x8x8(acc[s & 1], ah[s], bl0, bl1);
+          mma_tf32_16x8x8(acc[s & 1], ah[s], bh0, bh1);
+        }
+        // partial dY^T: d0 = (m2 g, edge 2t), d1 = (g, 2t+1), d2 = (g+8, 2t), d3 = (g+8, 2t+1)
+        float* rp = red + ((size_t)par * kTMCons + warp) * kBatch * kTMRedPitch;
+        rp[(2 * tq) * kTMRedPitch + g] = acc[0][0] + acc[1][0];
+        rp[(2 * tq + 1) * kTMRedPitch + g] = acc[0][1] + acc[1][1];
+        rp[(2 * tq) * kTMRedPitch + g + 8] = acc[0][2] + acc[1][2];
+        rp[(2 * tq + 1) * kTMRedPitch + g + 8] = acc[0][3] + acc[1][3];
+        __syncwarp();
+        if (lane == 0) {
+          tc::mbar_arrive(&empty[buf]);
+          tc::mbar_arrive(&red_full[par]);
+        }
+      }
+    }
+  }
+  __syncthreads();
+}
+
 template <int MODE>
 static int launch_aggregate(const float* F, int CF, const float* vec, const int64_t* other, const int64_t* row_ptr,
                             const int64_t* perm, float* slots, int64_t N, int64_t NF, const float* escale,
@@ -1227,15 +1551,12 @@ int bm_layer_bwd_targets(const float* x, const float* v, const float* W, const i
       ps[g] = MixSlots{Gt + (size_t)N * g * g * CPo, N * (2 * g + 1), CPo, Ws + pack_group_offset(kPackDs, g, Ci, Co),
                  kGroupPaths[g] * CPi, dS + slot_group_offset(g, N, CPi)};
     if ((rc = run_mix4(ps, st))) return rc;
-    if (Ci <= 64 && NS * (int64_t)Ci < (int64_t(1) << 31)) {
-      // x viewed as N * Ci rows of 16 floats; one box = the 64-byte rows of one atom
-      CUtensorMap xmap;
-      if ((rc = tc::encode_tmap(&xmap, tc::Operand{x, 16, NS * Ci, 64}, 16, Ci, 2))) return rc;
-      if ((rc = set_smem((const void*)layer_target_ws_kernel, kTSmem))) return rc;
+    if (Ci <= 64) {
+      if ((rc = set_smem((const void*)layer_target_mma_kernel, kTMSmem))) return rc;
       int* err = tc::error_flag();
       if (!err) return set_error(BM_ERR_CUDA, "layer_bwd: device error flag unavailable");
-      layer_target_ws_kernel<<<(unsigned)imin64(N, kNumSMs), kTThreads, kTSmem, st>>>(
-          xmap, dS, Ci, CPi, v, src, rpd, pd, gv, N, NS, edge_scale, grad_scale, err);
+      layer_target_mma_kernel<<<(unsigned)imin64(N, kNumSMs), kTMThreads, kTMSmem, st>>>(
+          x, dS, Ci, CPi, v, src, rpd, pd, gv, N, NS, edge_scale, grad_scale, err);
     } else {
       if ((rc = set_smem((const void*)layer_target_bwd_kernel, kTargetSmem))) return rc;
       layer_target_bwd_kernel<<<(unsigned)N, kLT, kTargetSmem, st>>>(dS, x, Ci, CPi, v, src, rpd, pd, gv, N, NS,
