@@ -51,35 +51,6 @@ __device__ __forceinline__ void ffma2(float2& d, float2 a, float2 b) {
   d.y = __uint_as_float((unsigned)(dd >> 32));
 }
 
-// Packed fp32 pair add (sm_100 f32x2): a + b lane-wise, one instruction.
-__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
-  unsigned long long aa = (unsigned long long)__float_as_uint(a.x) | ((unsigned long long)__float_as_uint(a.y) << 32);
-  const unsigned long long bb =
-      (unsigned long long)__float_as_uint(b.x) | ((unsigned long long)__float_as_uint(b.y) << 32);
-  asm("add.rn.f32x2 %0, %0, %1;" : "+l"(aa) : "l"(bb));
-  return make_float2(__uint_as_float((unsigned)aa), __uint_as_float((unsigned)(aa >> 32)));
-}
-
-// Two fp32 values in one 64-bit register pair, the operand form of the sm_100
-// f32x2 instructions; kept packed through hot loops so no repacking is needed.
-typedef unsigned long long f2x;
-__device__ __forceinline__ float2 f2x_unpack(f2x v) {
-  float2 r;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
-  return r;
-}
-__device__ __forceinline__ f2x f2x_dup(float v) {
-  f2x r;
-  asm("mov.b64 %0, {%1, %1};" : "=l"(r) : "f"(v));
-  return r;
-}
-__device__ __forceinline__ void f2x_fma(f2x& d, f2x a, f2x b) { asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(a), "l"(b)); }
-__device__ __forceinline__ f2x f2x_add(f2x a, f2x b) {
-  f2x r;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-
 // Warp-level tf32 tensor-core MMA (mma.sync m16n8k8, fp32 accumulate) and the
 // hi/lo split of an fp32 operand for the 3-pass product hi*hi + hi*lo + lo*hi
 // (about fp32 accuracy).  Fragment layout (g = lane / 4, t = lane % 4):

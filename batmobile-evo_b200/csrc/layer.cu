@@ -5,7 +5,7 @@
 // with Y_e = SH_3(v_e / max(|v_e|, 1e-8)).
 //
 // Because W does not depend on the edge, the sums are reordered:
-//   B_n[ci, m1, m2] = sum_{e -> n} x[src(e), ci, m1] Y_e[m2]            (edge loop, registers)
+//   B_n[ci, m1, m2] = sum_{e -> n} x[src(e), ci, m1] Y_e[m2]            (edge loop, 3xTF32 mma.sync)
 //   S_n[p, mo, ci]  = sum_{(m1,m2,mo) in p} c B_n[ci, m1, m2]            (CG, shared memory)
 //   out[n, co, mo]  = sum_{p, ci} S_n[p, mo, ci] W[p, ci, co]           (grouped GEMM)
 // so neither Y_e nor the per-edge messages are ever written to HBM, the scatter
@@ -15,7 +15,7 @@
 // Backward:
 //   dW = sum_n S_n^T G_n                        (split-K GEMM, deterministic sum)
 //   dS_n = G_n W^T                              (grouped GEMM)
-//   dB_n = CG^T dS_n ; dY_e = sum x[src] dB_n   (target pass, per edge) -> dv_e
+//   dB_n = CG^T dS_n ; dY_e = sum x[src] dB_n   (target pass, per edge, 3xTF32 mma.sync) -> dv_e
 //   dx_s: the same edge-sum/CG/GEMM machinery run over the SOURCE-sorted CSR
 //         with G[dst] in place of x and the CG grouped by l1 (no atomics).
 #include "mix_gemm.cuh"
@@ -105,9 +105,6 @@ __device__ __forceinline__ void contract_part(const float* __restrict__ Bs, int 
 //                      release it (bempty[tile]), overlapped with the
 //                      consumers' next atom.
 // kBatch divides 32 (the producers' edge groups).
-#ifndef BM_TGT_PAIR
-#define BM_TGT_PAIR 0
-#endif
 #ifndef BM_AGG_MQ
 #define BM_AGG_MQ 4
 #endif
@@ -140,22 +137,6 @@ constexpr int kContrWarps = 4;
 constexpr int kAggProdWarp0 = kLT / 32 + kContrWarps;
 constexpr size_t kAggSmem = (size_t)kRing * kSlotBytes + 2 * kBsBytes + 16;
 constexpr int kAggThreads = kLT + 32 * (kContrWarps + kProdWarps);
-
-__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kLT) : "memory"); }
-// consumer_sync that also ORs a flag over all consumer threads (bar.red.or):
-// every consumer warp leaves a pipeline together when any of them gave up.
-__device__ __forceinline__ bool consumer_sync_or(bool v) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 q, %1, 0;\n\t"
-      "bar.red.or.pred p, 1, %2, q;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(r)
-      : "r"((uint32_t)v), "n"(kLT)
-      : "memory");
-  return r != 0;
-}
 
 // Bounded spin until *turn == want; false (and *err set) after a few seconds.
 __device__ __forceinline__ bool wait_turn(const uint32_t* turn, uint32_t want, int* err) {
@@ -675,38 +656,9 @@ static int set_smem(const void* fn, size_t bytes) {
   return BM_OK;
 }
 
-// ---------------------------------------------------------------------------
-// Target-side backward, warp-specialised (C_in <= 64).  Persistent CTAs (one
-// per SM) walk the atoms n_k = blockIdx.x + k * gridDim.x that have edges:
-//   warps 8-10 (producers)  warp w serves the atoms k = w (mod 3); in stream
-//                           order it loads the atom's dS block (bulk copies into
-//                           a [156][64] shared tile) and then its edges in
-//                           batches of kBatch: per edge the edge index, raw
-//                           vector and a source flag into the slot's metadata
-//                           and the source's x row by a 2D TMA copy (64-byte
-//                           swizzle: 64 channel rows of 64 bytes);
-//   warps 0-7 (consumers)   per atom they build dB[c, m1, m2] = CG^T dS (warp
-//                           w: m2 quarter w % 4 for 32 channels, warp-uniform CG
-//                           code) into a swizzled shared tile, then each lane
-//                           takes the dB slice of its (channel 8 w + lane / 4, m2
-//                           quarter lane % 4) into registers; per edge
-//                             dY_e[m2] = sum_{c, m1} x[src e, c, m1] dB[c, m1, m2]
-//                           is 32 packed FMAs (m1 pairs) per lane, a 3-shuffle
-//                           reduce-scatter over the warp's 8 channels and one
-//                           partial per channel block in shared memory;
-//   warp 11 (epilogue)      per batch: adds the 8 channel-block partials and
-//                           applies the SH and normalisation chain rule -> dv_e.
-// Consumers and the epilogue hand partials over through mbarriers (two
-// parities), so the edge stream has no CTA-wide barrier.
-// ---------------------------------------------------------------------------
+// Shared by the target-side kernels below.
 constexpr int kTBufs = 3;                                 // batch buffers in the ring
-constexpr int kTRowBytes = 64 * 64;                       // x row: 64 channels x 16 floats
 constexpr size_t kTdSBytes = (size_t)kSlots * 64 * 4;     // dS block of one atom (pitch <= 64)
-constexpr size_t kTdBBytes = (size_t)64 * 4 * 16 * 16;       // dB tile: 64 channels x 4 quarters x 16 chunks
-constexpr size_t kTSmem = (size_t)kTBufs * kBatch * kTRowBytes + kTdSBytes + kTdBBytes + 1024;
-constexpr int kTProd = 3;                                 // producer warps
-constexpr int kTEpiWarp = kLT / 32 + kTProd;            // chain-rule warp
-constexpr int kTThreads = kLT + 32 * kTProd + 32;
 
 struct TMeta {  // per-slot edge metadata
   int64_t e;
@@ -745,354 +697,6 @@ __device__ __forceinline__ void dB_quarter(const float* __restrict__ dSs, int c,
 #undef BM_F
 }
 
-// dB tile in shared memory for the edge loop: per channel c and m2 quarter q,
-// 32 float2 pairs (dB[c, 2p, 4q+m], dB[c, 2p+1, 4q+m]) at pair index 4p + m,
-// stored as 16 chunks of 16 bytes with chunk k at k ^ ((c + 2q) & 7) so that
-// both the builder (32 channels, one q) and the readers (8 channels x 4 q) hit
-// distinct banks.
-__device__ __forceinline__ float4* dbt_chunk(float4* tile, int c, int q, int k) {
-  return tile + (c * 4 + q) * 16 + (k ^ ((c + 2 * q) & 7));
-}
-
-// Builds dB for m2 quarter Q (warp-uniform: lane = channel) and stores it in the tile.
-template <int Q>
-__device__ __forceinline__ void target_build_dB(const float* dSs, float4* tile, int c, bool cv) {
-  float2 d[16][2];  // [m1][m2 pair within the quarter]
-#pragma unroll
-  for (int i = 0; i < 16; ++i) d[i][0] = d[i][1] = make_float2(0.0f, 0.0f);
-  if (cv) dB_quarter<Q>(dSs, c, d);
-#pragma unroll
-  for (int k = 0; k < 16; ++k) {
-    // chunk k holds pairs 2k, 2k+1 = (p, m) = (k / 2, 2 (k % 2)) and (k / 2, 2 (k % 2) + 1)
-    const int p = k >> 1, m = 2 * (k & 1);
-    const float v0 = m == 0 ? d[2 * p][0].x : d[2 * p][1].x;
-    const float v1 = m == 0 ? d[2 * p + 1][0].x : d[2 * p + 1][1].x;
-    const float v2 = m == 0 ? d[2 * p][0].y : d[2 * p][1].y;
-    const float v3 = m == 0 ? d[2 * p + 1][0].y : d[2 * p + 1][1].y;
-    *dbt_chunk(tile, c, Q, k) = make_float4(v0, v1, v2, v3);
-  }
-}
-
-// 12 warps x 168 registers fit the register file (warps are allocated in groups
-// of four; the per-lane dB tile needs most of the registers).
-__global__ void __maxnreg__(168)
-layer_target_ws_kernel(const __grid_constant__ CUtensorMap xmap, const float* __restrict__ dS, int Ci, int CPi,
-                       const float* __restrict__ vec, const int64_t* __restrict__ src,
-                       const int64_t* __restrict__ row_ptr, const int64_t* __restrict__ perm,
-                       float* __restrict__ gv, int64_t N, int64_t NX, const float* __restrict__ escale,
-                       float* __restrict__ gscale, int* err) {
-  extern __shared__ __align__(16) uint8_t tsm_raw[];
-  uint8_t* tsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tsm_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* ring = tsm;                                                       // [kTBufs * kBatch][64 rows][64 B]
-  float* dSs = reinterpret_cast<float*>(tsm + (size_t)kTBufs * kBatch * kTRowBytes);  // [156][64]
-  float4* dbt = reinterpret_cast<float4*>(tsm + (size_t)kTBufs * kBatch * kTRowBytes + kTdSBytes);  // dB tile
-  __shared__ TMeta meta[kTBufs * kBatch];
-  __shared__ __align__(16) float red[2][kBatch][8][16];  // [batch parity][edge][channel block][m2]
-  __shared__ uint64_t full[kTBufs], empty[kTBufs], dfull, dempty, red_full[2], red_empty[2];
-  __shared__ uint32_t turn;
-  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  if (t == 0) {
-    turn = 0;
-    for (int i = 0; i < kTBufs; ++i) {
-      tc::mbar_init(&full[i], 1);
-      tc::mbar_init(&empty[i], kLT / 32 + 1);  // consumers + epilogue
-    }
-    tc::mbar_init(&dfull, 1);
-    tc::mbar_init(&dempty, kLT / 32);
-    for (int i = 0; i < 2; ++i) {
-      tc::mbar_init(&red_full[i], kLT / 32);
-      tc::mbar_init(&red_empty[i], 1);
-    }
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  // zero the x ring once: rows past C_in are never written by the row copies,
-  // and the edge loop reads every channel row without masking
-  for (int i = t; i < kTBufs * kBatch * kTRowBytes / 16; i += blockDim.x)
-    reinterpret_cast<float4*>(ring)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-  tc::fence_proxy_async_smem();
-  __syncthreads();
-  bool ok = true;
-  const uint32_t row_bytes = (uint32_t)Ci * 64u;
-
-  if (warp >= kLT / 32 && warp < kTEpiWarp) {
-    // ----------------------------------------------------------- producers
-    const int pw = warp - kLT / 32;
-    const int64_t step = gridDim.x;
-    uint32_t bi = 0, ac = 0;
-    {
-      uint32_t nb, na;
-      target_atom_counts(row_ptr, blockIdx.x + lane * step, N, nb, na);
-      if (lane >= pw) nb = na = 0;
-      bi = __reduce_add_sync(0xffffffffu, nb);
-      ac = __reduce_add_sync(0xffffffffu, na);
-    }
-    for (int64_t n = blockIdx.x + pw * step; n < N && ok; n += kTProd * step) {
-      const int64_t eb = row_ptr[n], ee = row_ptr[n + 1];
-      if (ee > eb) {
-        // dS block of the atom, in stream order just before its first batch
-        if (lane == 0) {
-          ok = wait_turn(&turn, bi, err);
-          if (ok && ac >= 1) ok = tc::mbar_wait(&dempty, (ac - 1) & 1, err);
-        }
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (ok) {
-          // shared layout [156][64]: one copy per l_out group when the channel
-          // pitch is 64, else one per slot row
-          if (CPi == 64) {
-            if (lane < 4) {
-              const int g = lane;
-              const uint32_t rows = (uint32_t)((2 * g + 1) * group_paths(g));
-              tc::bulk_g2s(dSs + (size_t)group_slot_off(g) * 64,
-                           dS + N * 64 * (int64_t)group_slot_off(g) + n * (int64_t)rows * 64, rows * 256u, &dfull);
-            }
-          } else {
-            for (int sl = lane; sl < kSlots; sl += 32) {
-              int g = 0;
-              while (g < 3 && sl >= group_slot_off(g + 1)) ++g;
-              const int local = sl - group_slot_off(g);
-              const int64_t rows = (2 * g + 1) * group_paths(g);
-              tc::bulk_g2s(dSs + (size_t)sl * 64, dS + N * CPi * (int64_t)group_slot_off(g) + (n * rows + local) * CPi,
-                           (uint32_t)CPi * 4u, &dfull);
-            }
-          }
-          __syncwarp();
-          if (lane == 0) tc::mbar_expect_tx(&dfull, (uint32_t)kSlots * (uint32_t)CPi * 4u);
-        }
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        ++ac;
-        for (int64_t g0 = eb; g0 < ee && ok; g0 += 32) {
-          const int gcnt = (int)imin64(32, ee - g0);
-          TMeta m{};
-          int64_t srow = -1;
-          if (lane < gcnt) {
-            const int64_t e = perm ? perm[g0 + lane] : g0 + lane;
-            const int64_t sidx = src[e];
-            srow = (sidx >= 0 && sidx < NX) ? sidx : -1;
-            m.e = e;
-            m.vx = vec[3 * e];
-            m.vy = vec[3 * e + 1];
-            m.vz = vec[3 * e + 2];
-            m.valid = srow >= 0 ? 1 : 0;
-            m.sc = escale ? escale[e] : 1.0f;
-          }
-          for (int b0 = 0; b0 < gcnt && ok; b0 += kBatch, ++bi) {
-            const int cnt = min(kBatch, gcnt - b0);
-            const bool act = lane >= b0 && lane < b0 + cnt;
-            const uint32_t buf = bi % kTBufs;
-            if (lane == 0) {
-              if (b0 > 0 || g0 > eb) ok = wait_turn(&turn, bi, err);  // the first batch holds the turn already
-              if (ok && bi >= kTBufs) ok = tc::mbar_wait(&empty[buf], ((bi / kTBufs) - 1) & 1, err);
-            }
-            ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok) break;
-            const uint32_t mine = (act && srow >= 0) ? row_bytes : 0u;
-            if (act) {
-              const int sl = buf * kBatch + (lane - b0);
-              meta[sl] = m;
-              if (srow >= 0)
-                tc::tma_load_2d(tc::smem_u32(ring + (size_t)sl * kTRowBytes), &xmap, 0, (int)(srow * Ci), &full[buf]);
-            }
-            const uint32_t total = __reduce_add_sync(0xffffffffu, mine);
-            __syncwarp();
-            if (lane == 0) {
-              tc::mbar_expect_tx(&full[buf], total);
-              *reinterpret_cast<volatile uint32_t*>(&turn) = bi + 1;
-            }
-          }
-        }
-      }
-      uint32_t nb = 0, na = 0;
-      if (lane >= 1 && lane < kTProd) target_atom_counts(row_ptr, n + lane * step, N, nb, na);
-      bi += __reduce_add_sync(0xffffffffu, nb);
-      ac += __reduce_add_sync(0xffffffffu, na);
-    }
-  } else if (warp == kTEpiWarp) {
-    // ------------------------------------------------------------ epilogue
-    // per batch: dY_e = sum of the 8 channel-block partials, then the SH and
-    // normalisation chain rule -> dv_e; lane = (edge lane / 4, m2 quarter lane % 4)
-    const int je = lane >> 2, mq = lane & 3;
-    uint32_t bi = 0;
-    for (int64_t n = blockIdx.x; n < N && ok; n += gridDim.x) {
-      const int64_t eb = row_ptr[n], ee = row_ptr[n + 1];
-      for (int64_t e0 = eb; e0 < ee && ok; e0 += kBatch, ++bi) {
-        const int cnt = (int)imin64(kBatch, ee - e0);
-        const uint32_t buf = bi % kTBufs, par = bi & 1;
-        if (!tc::mbar_wait(&red_full[par], (bi >> 1) & 1, err)) { ok = false; break; }
-        float4 dq = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int w = 0; w < 8; ++w) {
-          const float4 r4 = *reinterpret_cast<const float4*>(&red[par][je][w][4 * mq]);
-          dq.x += r4.x; dq.y += r4.y; dq.z += r4.z; dq.w += r4.w;
-        }
-        float dyv[16];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int srcl = (lane & ~3) + k;
-          dyv[4 * k] = __shfl_sync(0xffffffffu, dq.x, srcl);
-          dyv[4 * k + 1] = __shfl_sync(0xffffffffu, dq.y, srcl);
-          dyv[4 * k + 2] = __shfl_sync(0xffffffffu, dq.z, srcl);
-          dyv[4 * k + 3] = __shfl_sync(0xffffffffu, dq.w, srcl);
-        }
-        if (mq == 0 && je < cnt) {
-          const TMeta mm = meta[buf * kBatch + je];
-          if (!mm.valid) {  // the ring slot of an invalid source holds stale rows
-#pragma unroll
-            for (int m2 = 0; m2 < 16; ++m2) dyv[m2] = 0.0f;
-          }
-          target_edge_epilogue(mm.e, mm.vx, mm.vy, mm.vz, mm.sc, dyv, gv, gscale);
-        }
-        __syncwarp();
-        if (lane == 0) {
-          tc::mbar_arrive(&red_empty[par]);
-          tc::mbar_arrive(&empty[buf]);
-        }
-      }
-    }
-  } else {
-    // ----------------------------------------------------------- consumers
-    float4* tile = dbt;
-    // edge-loop mapping: warp w owns channels 8w .. 8w+7, lane = (channel, m2 quarter)
-    const int qq = lane & 3, ce = 8 * warp + (lane >> 2);
-    const int sw = (ce >> 1) & 3;  // 64-byte swizzle of channel row ce
-    const bool hi16 = lane & 16, h8 = lane & 8;
-#if BM_TGT_PAIR
-    const bool pm_hi = h8, pm_lo = lane & 4;  // reduce-scatter stages over lane bits 16 (edge), 8, 4 (m2)
-#else
-    const bool pm_hi = hi16, pm_lo = h8;      // stages over lane bits 16, 8 (m2), then a sum over bit 4
-#endif
-    const int red_m2 = 4 * qq + (pm_hi ? 2 : 0) + (pm_lo ? 1 : 0);  // m2 of this lane's reduced value
-    uint32_t bi = 0, ac = 0;
-    bool stuck = false;  // a bounded wait of this warp gave up in the edge loop (warp-uniform)
-    for (int64_t n = blockIdx.x; n < N && ok; n += gridDim.x) {
-      const int64_t eb = row_ptr[n], ee = row_ptr[n + 1];
-      if (ee <= eb) continue;
-      const bool gave_up = stuck || !tc::mbar_wait(&dfull, ac & 1, err);
-      ++ac;
-      // every warp is done reading the previous atom's tile; if any consumer
-      // thread gave up on a wait, all consumer warps leave here together
-      if (consumer_sync_or(gave_up)) { ok = false; break; }
-      {
-        const int cb = (warp >> 2) * 32 + lane;
-        const bool cbv = cb < Ci;
-        switch (warp & 3) {
-          case 0: target_build_dB<0>(dSs, tile, cb, cbv); break;
-          case 1: target_build_dB<1>(dSs, tile, cb, cbv); break;
-          case 2: target_build_dB<2>(dSs, tile, cb, cbv); break;
-          default: target_build_dB<3>(dSs, tile, cb, cbv); break;
-        }
-      }
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&dempty);
-      consumer_sync();
-      // d2[p][j] = (dB[ce, 2p, m], dB[ce, 2p+1, m]) with m = 4 qq + (j ^ pm): the lane's
-      // m2 order is permuted by its reduce-scatter position (pm), so that at each
-      // shuffle stage every lane keeps its low local values and sends the high ones
-      // (no lane-dependent selects in the edge loop)
-      f2x d2[8][4];
-#pragma unroll
-      for (int p = 0; p < 8; ++p) {
-        const ulonglong2 lo = *reinterpret_cast<const ulonglong2*>(dbt_chunk(tile, ce, qq, 2 * p + (pm_hi ? 1 : 0)));
-        const ulonglong2 up = *reinterpret_cast<const ulonglong2*>(dbt_chunk(tile, ce, qq, 2 * p + (pm_hi ? 0 : 1)));
-        d2[p][0] = pm_lo ? lo.y : lo.x;
-        d2[p][1] = pm_lo ? lo.x : lo.y;
-        d2[p][2] = pm_lo ? up.y : up.x;
-        d2[p][3] = pm_lo ? up.x : up.y;
-      }
-      for (int64_t e0 = eb; e0 < ee && !stuck; e0 += kBatch, ++bi) {
-        const int cnt = (int)imin64(kBatch, ee - e0);
-        const uint32_t buf = bi % kTBufs, par = bi & 1;
-        // warp votes: the warp stays converged and meets the others at the next consumer_sync_or
-        if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[buf], (bi / kTBufs) & 1, err))) { stuck = true; break; }
-        // red[par] is free once the epilogue has finished the batch two back
-        if (bi >= 2 && !__all_sync(0xffffffffu, tc::mbar_wait(&red_empty[par], ((bi >> 1) - 1) & 1, err))) {
-          stuck = true;
-          break;
-        }
-        // rows of invalid sources and channels >= C_in hold finite data (the ring
-        // starts zeroed); the epilogue drops invalid edges, dB is zero past C_in
-        const uint8_t* row0 = ring + (size_t)(buf * kBatch) * kTRowBytes + ce * 64;
-#if BM_TGT_PAIR
-        // two edges per step: lanes with bit 16 set take them in the other order,
-        // so the 8 partials reduce-scatter to one (edge, m2) value per lane
-        for (int j = 0; j < cnt; j += 2) {
-          const ulonglong2* ra = reinterpret_cast<const ulonglong2*>(row0 + (size_t)(j + (hi16 ? 1 : 0)) * kTRowBytes);
-          const ulonglong2* rb = reinterpret_cast<const ulonglong2*>(row0 + (size_t)(j + (hi16 ? 0 : 1)) * kTRowBytes);
-          f2x a[2][4], b[2][4];
-#pragma unroll
-          for (int h = 0; h < 2; ++h)
-#pragma unroll
-            for (int m = 0; m < 4; ++m) a[h][m] = b[h][m] = 0ull;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const ulonglong2 xa = ra[i ^ sw], xb = rb[i ^ sw];
-#pragma unroll
-            for (int m = 0; m < 4; ++m) {
-              f2x_fma(a[i >> 1][m], xa.x, d2[2 * i][m]);
-              f2x_fma(b[i >> 1][m], xb.x, d2[2 * i][m]);
-              f2x_fma(a[i >> 1][m], xa.y, d2[2 * i + 1][m]);
-              f2x_fma(b[i >> 1][m], xb.y, d2[2 * i + 1][m]);
-            }
-          }
-          float va[4], vb[4];
-#pragma unroll
-          for (int m = 0; m < 4; ++m) {
-            const float2 sa = f2x_unpack(f2x_add(a[0][m], a[1][m]));
-            const float2 sb = f2x_unpack(f2x_add(b[0][m], b[1][m]));
-            va[m] = sa.x + sa.y;
-            vb[m] = sb.x + sb.y;
-          }
-          float k[4];
-#pragma unroll
-          for (int m = 0; m < 4; ++m) k[m] = va[m] + __shfl_xor_sync(0xffffffffu, vb[m], 16);
-          const float k0 = k[0] + __shfl_xor_sync(0xffffffffu, k[2], 8);
-          const float k1 = k[1] + __shfl_xor_sync(0xffffffffu, k[3], 8);
-          const float r = k0 + __shfl_xor_sync(0xffffffffu, k1, 4);
-          const int je = j + (hi16 ? 1 : 0);
-          if (je < cnt) red[par][je][warp][red_m2] = r;
-        }
-#else
-#pragma unroll 2
-        for (int j = 0; j < cnt; ++j) {
-          const ulonglong2* row = reinterpret_cast<const ulonglong2*>(row0 + (size_t)j * kTRowBytes);
-          f2x a[2][4];
-#pragma unroll
-          for (int h = 0; h < 2; ++h)
-#pragma unroll
-            for (int m = 0; m < 4; ++m) a[h][m] = 0ull;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const ulonglong2 x2 = row[i ^ sw];
-#pragma unroll
-            for (int m = 0; m < 4; ++m) {
-              f2x_fma(a[i >> 1][m], x2.x, d2[2 * i][m]);
-              f2x_fma(a[i >> 1][m], x2.y, d2[2 * i + 1][m]);
-            }
-          }
-          float v[4];
-#pragma unroll
-          for (int m = 0; m < 4; ++m) {
-            const float2 s2 = f2x_unpack(f2x_add(a[0][m], a[1][m]));
-            v[m] = s2.x + s2.y;
-          }
-          // reduce-scatter over the warp's 8 channels (lanes with equal qq)
-          const float k0 = v[0] + __shfl_xor_sync(0xffffffffu, v[2], 16);
-          const float k1 = v[1] + __shfl_xor_sync(0xffffffffu, v[3], 16);
-          float r = k0 + __shfl_xor_sync(0xffffffffu, k1, 8);
-          r += __shfl_xor_sync(0xffffffffu, r, 4);
-          if ((lane & 4) == 0) red[par][j][warp][red_m2] = r;
-        }
-#endif
-        __syncwarp();
-        if (lane == 0) {
-          tc::mbar_arrive(&empty[buf]);
-          tc::mbar_arrive(&red_full[par]);
-        }
-      }
-    }
-  }
-  __syncthreads();
-}
-
 // ---------------------------------------------------------------------------
 // Target-side backward on warp-level tensor cores (C_in <= 64).  Per target
 // atom n the edge gradient is a product with K = 1024 rows (channel, m1):
@@ -1100,27 +704,28 @@ layer_target_ws_kernel(const __grid_constant__ CUtensorMap xmap, const float* __
 // i.e. per batch of 8 edges an [16 x 1024] x [1024 x 8] product (mma.sync
 // m16n8k8 tf32, M = m2, N = edges, 3xTF32: hi*hi + hi*lo + lo*hi).
 // Persistent CTAs (one per SM) walk the atoms n_k = blockIdx.x + k * gridDim.x:
-//   warps 16-18 (producers)  as in the SIMT kernel: per atom the dS block by
+//   warps 16-17 (producers)  as in the SIMT kernel: per atom the dS block by
 //                            bulk copies, then its edges in batches of kBatch
 //                            (metadata + the source's x row, one bulk copy of
 //                            C_in x 64 bytes into a slot padded to 4 mod 32
 //                            words, so a fragment load of 8 edges x 4 K hits 32
 //                            banks);
-//   warps 0-15 (consumers)   per atom warps 0-7 build dB = CG^T dS (warp w: m2
-//                            quarter w % 4 for 32 channels) into a [m2][K]
-//                            tile; every warp w then keeps the A fragments of its
+//   warps 0-15 (consumers)   per atom they build dB = CG^T dS (warp w: m2
+//                            quarter w % 4, 32 channels, m1 half w / 8) into a
+//                            [m2][K] tile; every warp w then keeps the A fragments of its
 //                            K slice 64 w .. 64 w + 63 (channels 4w .. 4w+3) in
 //                            registers, split into tf32 hi/lo (64 registers);
 //                            per batch: 8 k-steps of 3 MMAs on the x fragments
 //                            (two loads per k-step), the warp's partial
 //                            dY^T[16 x 8] into shared memory;
-//   warp 19 (epilogue)       per batch: adds the 16 K-slice partials and applies
-//                            the SH and normalisation chain rule -> dv_e.
+//   warps 18-19 (epilogue)   per batch (one warp per batch parity): adds the 16
+//                            K-slice partials and applies the SH and
+//                            normalisation chain rule -> dv_e.
 // ---------------------------------------------------------------------------
 constexpr int kTMCons = 16;                                  // consumer warps (K slices of 64)
-constexpr int kTMProd = 3;                                   // producer warps
-constexpr int kTMEpi = kTMCons + kTMProd;                    // epilogue warp
-constexpr int kTMThreads = 32 * (kTMCons + kTMProd + 1);
+constexpr int kTMProd = 2;                                   // producer warps
+constexpr int kTMEpi = kTMCons + kTMProd;                    // first epilogue warp
+constexpr int kTMThreads = 32 * (kTMCons + kTMProd + 2);     // two epilogue warps (one per batch parity)
 constexpr int kTMSlot = 4096 + 16;                           // x row slot (bytes): 4 mod 32 words
 constexpr int kTMdBPitch = 1028;                             // dB tile [m2][K] row pitch (floats)
 constexpr int kTMRedPitch = 20;                              // partials [warp][edge][m2 (+pad)]
@@ -1151,17 +756,37 @@ __device__ __forceinline__ int dbk_off(int m2, int c, int m1) {
   return m2 * kTMdBPitch + c * 16 + 4 * ((m1 >> 2) ^ ((c >> 1) & 3)) + (m1 & 3);
 }
 
-// Builds dB for m2 quarter Q (warp-uniform, lane = channel c) into the [m2][K] tile.
-template <int Q>
+// dB[c, m1, m2] for m2 quarter Q and m1 in 8 H .. 8 H + 7 (compile-time filter
+// on the CG list of the quarter).
+template <int Q, int H>
+__device__ __forceinline__ void dB_quarter_half(const float* __restrict__ dSs, int c, float2 (&d)[16][2]) {
+  const float* col = dSs + c;
+#define BM_X(m1, j, slot, coeff)                                                \
+  if ((m1) >= 8 * H && (m1) < 8 * H + 8) {                                      \
+    float& r_ = ((j) & 1) ? d[m1][(j) >> 1].y : d[m1][(j) >> 1].x;              \
+    r_ = fmaf((coeff), col[(slot) * 64], r_);                                   \
+  }
+#define BM_F() asm volatile("" ::: "memory");
+  if constexpr (Q == 0) { BM_CG_M2Q_0(BM_X, BM_F) }
+  if constexpr (Q == 1) { BM_CG_M2Q_1(BM_X, BM_F) }
+  if constexpr (Q == 2) { BM_CG_M2Q_2(BM_X, BM_F) }
+  if constexpr (Q == 3) { BM_CG_M2Q_3(BM_X, BM_F) }
+#undef BM_X
+#undef BM_F
+}
+
+// Builds dB for m2 quarter Q and m1 half H (warp-uniform, lane = channel c)
+// into the [m2][K] tile.
+template <int Q, int H>
 __device__ __forceinline__ void target_build_dBk(const float* dSs, float* dBt, int c, bool cv) {
   float2 d[16][2];  // [m1][m2 pair within the quarter]
 #pragma unroll
   for (int i = 0; i < 16; ++i) d[i][0] = d[i][1] = make_float2(0.0f, 0.0f);
-  if (cv) dB_quarter<Q>(dSs, c, d);
+  if (cv) dB_quarter_half<Q, H>(dSs, c, d);
 #pragma unroll
   for (int m = 0; m < 4; ++m)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 2 * H; j < 2 * H + 2; ++j) {
       float v[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) v[u] = (m & 1) ? d[4 * j + u][m >> 1].y : d[4 * j + u][m >> 1].x;
@@ -1191,7 +816,7 @@ layer_target_mma_kernel(const float* __restrict__ x, const float* __restrict__ d
       tc::mbar_init(&empty[i], kTMCons + 1);  // consumers + epilogue
     }
     tc::mbar_init(&dfull, 1);
-    tc::mbar_init(&dempty, 8);  // the eight builder warps
+    tc::mbar_init(&dempty, kTMCons);  // every consumer warp builds a part of dB
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&red_full[i], kTMCons);
       tc::mbar_init(&red_empty[i], 1);
@@ -1206,6 +831,10 @@ layer_target_mma_kernel(const float* __restrict__ x, const float* __restrict__ d
   __syncthreads();
   bool ok = true;
   const uint32_t row_bytes = (uint32_t)Ci * 64u;
+#ifdef BM_LDIAG
+  constexpr int MODE = 0;
+#endif
+  LD_DECL
 
   if (warp >= kTMCons && warp < kTMEpi) {
     // ----------------------------------------------------------- producers
@@ -1222,10 +851,12 @@ layer_target_mma_kernel(const float* __restrict__ x, const float* __restrict__ d
     for (int64_t n = blockIdx.x + pw * step; n < N && ok; n += kTMProd * step) {
       const int64_t eb = row_ptr[n], ee = row_ptr[n + 1];
       if (ee > eb) {
+        LD_MARK()
         if (lane == 0) {
           ok = wait_turn(&turn, bi, err);
           if (ok && ac >= 1) ok = tc::mbar_wait(&dempty, (ac - 1) & 1, err);
         }
+        LD_ADD(8)
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (ok) {
           if (CPi == 64) {
@@ -1269,10 +900,12 @@ layer_target_mma_kernel(const float* __restrict__ x, const float* __restrict__ d
             const int cnt = min(kBatch, gcnt - b0);
             const bool act = lane >= b0 && lane < b0 + cnt;
             const uint32_t buf = bi % kTBufs;
+            LD_MARK()
             if (lane == 0) {
               if (b0 > 0 || g0 > eb) ok = wait_turn(&turn, bi, err);  // the first batch holds the turn already
               if (ok && bi >= kTBufs) ok = tc::mbar_wait(&empty[buf], ((bi / kTBufs) - 1) & 1, err);
             }
+            LD_ADD(9)
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             const uint32_t mine = (act && srow >= 0) ? row_bytes : 0u;
@@ -1295,18 +928,24 @@ layer_target_mma_kernel(const float* __restrict__ x, const float* __restrict__ d
       bi += __reduce_add_sync(0xffffffffu, nb);
       ac += __reduce_add_sync(0xffffffffu, na);
     }
-  } else if (warp == kTMEpi) {
+    LD_FLUSH(10)
+  } else if (warp >= kTMEpi) {
     // ------------------------------------------------------------ epilogue
-    // per batch: dY_e = sum of the 16 K-slice partials, then the SH and
-    // normalisation chain rule -> dv_e; lane = (edge lane / 4, m2 quarter lane % 4)
+    // warp kTMEpi + p takes the batches of parity p: dY_e = sum of the 16 K-slice
+    // partials, then the SH and normalisation chain rule -> dv_e; lane = (edge
+    // lane / 4, m2 quarter lane % 4)
     const int je = lane >> 2, mq = lane & 3;
+    const uint32_t mine = (uint32_t)(warp - kTMEpi);
     uint32_t bi = 0;
     for (int64_t n = blockIdx.x; n < N && ok; n += gridDim.x) {
       const int64_t eb = row_ptr[n], ee = row_ptr[n + 1];
       for (int64_t e0 = eb; e0 < ee && ok; e0 += kBatch, ++bi) {
         const int cnt = (int)imin64(kBatch, ee - e0);
         const uint32_t buf = bi % kTBufs, par = bi & 1;
+        if (par != mine) continue;
+        LD_MARK()
         if (!tc::mbar_wait(&red_full[par], (bi >> 1) & 1, err)) { ok = false; break; }
+        LD_ADD(11)
         const float* rp = red + (size_t)par * kTMCons * kBatch * kTMRedPitch + je * kTMRedPitch + 4 * mq;
         float4 dq = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
@@ -1332,12 +971,14 @@ layer_target_mma_kernel(const float* __restrict__ x, const float* __restrict__ d
           target_edge_epilogue(mm.e, mm.vx, mm.vy, mm.vz, mm.sc, dyv, gv, gscale);
         }
         __syncwarp();
+        LD_ADD(12)
         if (lane == 0) {
           tc::mbar_arrive(&red_empty[par]);
           tc::mbar_arrive(&empty[buf]);
         }
       }
     }
+    LD_FLUSH(13)
   } else {
     // ----------------------------------------------------------- consumers
     const int g = lane >> 2, tq = lane & 3;
@@ -1346,24 +987,29 @@ layer_target_mma_kernel(const float* __restrict__ x, const float* __restrict__ d
     for (int64_t n = blockIdx.x; n < N && ok; n += gridDim.x) {
       const int64_t eb = row_ptr[n], ee = row_ptr[n + 1];
       if (ee <= eb) continue;
-      const bool gave_up = stuck || !__all_sync(0xffffffffu, warp >= 8 || tc::mbar_wait(&dfull, ac & 1, err));
+      LD_MARK()
+      const bool gave_up = stuck || !__all_sync(0xffffffffu, tc::mbar_wait(&dfull, ac & 1, err));
       ++ac;
       // every warp is done with the previous atom's tile; if any consumer gave
       // up on a wait, all consumer warps leave here together
       if (cons16_sync_or(gave_up)) { ok = false; break; }
-      if (warp < 8) {
-        const int cb = (warp >> 2) * 32 + lane;
+      LD_ADD(0)
+      {
+        // warp w builds m2 quarter w % 4, channels 32 ((w / 4) % 2) + lane, m1 half w / 8
+        const int cb = ((warp >> 2) & 1) * 32 + lane;
         const bool cbv = cb < Ci;
         switch (warp & 3) {
-          case 0: target_build_dBk<0>(dSs, dBt, cb, cbv); break;
-          case 1: target_build_dBk<1>(dSs, dBt, cb, cbv); break;
-          case 2: target_build_dBk<2>(dSs, dBt, cb, cbv); break;
-          default: target_build_dBk<3>(dSs, dBt, cb, cbv); break;
+          case 0: if (warp < 8) target_build_dBk<0, 0>(dSs, dBt, cb, cbv); else target_build_dBk<0, 1>(dSs, dBt, cb, cbv); break;
+          case 1: if (warp < 8) target_build_dBk<1, 0>(dSs, dBt, cb, cbv); else target_build_dBk<1, 1>(dSs, dBt, cb, cbv); break;
+          case 2: if (warp < 8) target_build_dBk<2, 0>(dSs, dBt, cb, cbv); else target_build_dBk<2, 1>(dSs, dBt, cb, cbv); break;
+          default: if (warp < 8) target_build_dBk<3, 0>(dSs, dBt, cb, cbv); else target_build_dBk<3, 1>(dSs, dBt, cb, cbv); break;
         }
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&dempty);
       }
+      LD_ADD(1)
       cons16_sync();
+      LD_ADD(2)
       // A fragments of this warp's K slice: k-step s covers channel 4 w + s / 2,
       // m1 = 8 (s % 2) + 0..7; a0 = dB^T[g][t], a1 = [g+8][t], a2 = [g][t+4], a3 = [g+8][t+4]
       uint32_t ah[8][4], al[8][4];
@@ -1375,15 +1021,19 @@ layer_target_mma_kernel(const float* __restrict__ x, const float* __restrict__ d
         split_tf32(dBt[dbk_off(g, c, m1 + 4)], ah[s][2], al[s][2]);
         split_tf32(dBt[dbk_off(g + 8, c, m1 + 4)], ah[s][3], al[s][3]);
       }
+      LD_ADD(3)
       for (int64_t e0 = eb; e0 < ee && !stuck; e0 += kBatch, ++bi) {
         const uint32_t buf = bi % kTBufs, par = bi & 1;
+        LD_MARK()
         // warp votes: the warp stays converged and meets the others at the next cons16_sync_or
         if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[buf], (bi / kTBufs) & 1, err))) { stuck = true; break; }
+        LD_ADD(4)
         // red[par] is free once the epilogue has finished the batch two back
         if (bi >= 2 && !__all_sync(0xffffffffu, tc::mbar_wait(&red_empty[par], ((bi >> 1) - 1) & 1, err))) {
           stuck = true;
           break;
         }
+        LD_ADD(5)
         // B fragments: b0 = x[src of slot g][K0 + t], b1 = [K0 + t + 4]; slots past
         // the batch hold finite stale rows whose results the epilogue drops
         const float* xs = reinterpret_cast<const float*>(ring + (size_t)(buf * kBatch + g) * kTMSlot) + 64 * warp + tq;
@@ -1404,12 +1054,14 @@ layer_target_mma_kernel(const float* __restrict__ x, const float* __restrict__ d
         rp[(2 * tq) * kTMRedPitch + g + 8] = acc[0][2] + acc[1][2];
         rp[(2 * tq + 1) * kTMRedPitch + g + 8] = acc[0][3] + acc[1][3];
         __syncwarp();
+        LD_ADD(6)
         if (lane == 0) {
           tc::mbar_arrive(&empty[buf]);
           tc::mbar_arrive(&red_full[par]);
         }
       }
     }
+    LD_FLUSH(7)
   }
   __syncthreads();
 }
