@@ -24,6 +24,7 @@ _SIGNATURES = {
     "bm_version": (_i32, []),
     "bm_launch_count": (_i64, []),
     "bm_probe_fp32": (_i32, [_p, _i32, _i32, _p]),
+    "bm_probe_mma_tf32": (_i32, [_p, _i32, _i32, _p]),
     "bm_set_mix_precision": (_i32, [_i32]),
     "bm_get_mix_precision": (_i32, []),
     "bm_device_error_check": (_i32, []),

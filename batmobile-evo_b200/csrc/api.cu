@@ -424,6 +424,37 @@ extern "C" int bm_probe_fp32(float* scratch, int iters, int blocks, void* stream
   return bm::check_launch("bm_probe_fp32");
 }
 
+// -------------------------------------------------- tensor-core probe --
+// Peak rate of the warp-level tf32 MMA (mma.sync m16n8k8, fp32 accumulate) on
+// this device, the unit the edge-sum and target passes run on: every warp
+// keeps 8 independent accumulators.
+namespace bm {
+__global__ void __launch_bounds__(256) mma_tf32_probe_kernel(float* out, int iters) {
+  float acc[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+  const uint32_t l = threadIdx.x;
+  const uint32_t a[4] = {__float_as_uint(1.0f + l), __float_as_uint(0.5f), __float_as_uint(0.25f), __float_as_uint(2.0f)};
+  const uint32_t b0 = __float_as_uint(1e-3f), b1 = __float_as_uint(-1e-3f);
+  for (int it = 0; it < iters; ++it) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mma_tf32_16x8x8(acc[i], a, b0, b1);
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) s += acc[i][0] + acc[i][1] + acc[i][2] + acc[i][3];
+  if (s == 123.456f) out[0] = s;  // keeps the chains live
+}
+}  // namespace bm
+
+extern "C" int bm_probe_mma_tf32(float* scratch, int iters, int blocks, void* stream) {
+  BM_REQUIRE(scratch && iters > 0 && blocks > 0, "bm_probe_mma_tf32: bad arguments");
+  bm::mma_tf32_probe_kernel<<<blocks, 256, 0, bm::as_stream(stream)>>>(scratch, iters);
+  return bm::check_launch("bm_probe_mma_tf32");
+}
+
 // ------------------------------------------------- bounded-wait self-test --
 // One thread waits on a shared-memory mbarrier that nothing ever arrives on,
 // through the same bounded wait every pipelined kernel of the library uses.

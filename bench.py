@@ -306,6 +306,26 @@ def probe_fp32_tflops(lib):
     return best
 
 
+def probe_mma_tf32_tflops(lib):
+    """Warp-level tf32 MMA rate (mma.sync m16n8k8) of this device, measured now."""
+    import ctypes
+    buf = torch.zeros(1, device="cuda")
+    iters, blocks = 2048, 148 * 4
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for _ in range(3):
+        lib.bm_probe_mma_tf32(ctypes.c_void_p(buf.data_ptr()), iters, blocks, st)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    best = 0.0
+    for _ in range(5):
+        s.record()
+        lib.bm_probe_mma_tf32(ctypes.c_void_p(buf.data_ptr()), iters, blocks, st)
+        e.record()
+        e.synchronize()
+        flop = 2.0 * 16 * 8 * 8 * 8 * iters * blocks * 8   # 8 warps x 8 MMAs of 16x8x8 per iteration
+        best = max(best, flop / (s.elapsed_time(e) * 1e-3) / 1e12)
+    return best
+
+
 def measured_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -315,35 +335,43 @@ def measured_peaks():
 
 
 def layer_work(E, n_targets, n_sources, c):
-    """Algorithmic work per launch (FLOP, bounding unit) of the layer's kernels:
-    256*C FMA per edge for the edge sums (outer products or dY), 611*C per atom
-    for the CG contraction, 156*C*C per atom for each channel mix."""
+    """Work per launch (FLOP, bounding unit) of the layer's kernels: 256*C FMA
+    per edge for the edge sums (outer products or dY), run as a 3xTF32 product
+    on the warp-level tensor cores (three tf32 MMAs per fp32 product: the
+    tensor work is 3 x 2 x 256*C*E), 611*C per atom for the CG contraction (SIMT),
+    156*C*C per atom for each channel mix."""
     return {
-        "layer_bwd(target)": (2.0 * 256 * c * E + 2.0 * 611 * c * n_targets, "fp32"),
-        "layer_fwd(aggregate)": (2.0 * 256 * c * E + 2.0 * 611 * c * n_targets, "fp32"),
-        "layer_bwd(source aggregate)": (2.0 * 256 * c * E + 2.0 * 611 * c * n_sources, "fp32"),
+        "layer_bwd(target)": (3 * 2.0 * 256 * c * E, "mma"),
+        "layer_fwd(aggregate)": (3 * 2.0 * 256 * c * E, "mma"),
+        "layer_bwd(source aggregate)": (3 * 2.0 * 256 * c * E, "mma"),
         "tc_gemm(mix->irreps)": (2.0 * 156 * c * c * (n_targets + n_sources) / 2.0, "tensor"),
         "tc_gemm(grad->slots)": (2.0 * 156 * c * c * n_targets, "tensor"),
         "tc_gemm(weight grad)": (2.0 * 156 * c * c * n_targets, "tensor"),
     }
 
 
-def roofline_of(kernels, work, fp32_peak, tf32_peak, peak_kind, peaks, traffic=None):
+def roofline_of(kernels, work, mma_peak, tf32_peak, peak_kind, peaks, traffic=None):
     """The dominant kernel's achieved FLOP/s against its unit's measured peak."""
     top = next((k for k in kernels if k["name"] in work), kernels[0])
-    flop, bound = work.get(top["name"], (0.0, "fp32"))
+    flop, bound = work.get(top["name"], (0.0, "mma"))
     achieved = flop / (top["ms_per_launch"] * 1e-3) / 1e12
-    peak = fp32_peak if bound == "fp32" else tf32_peak
-    return {
-        "bound": bound, "unit": "TFLOP/s", "achieved": achieved, "peak": peak, "frac": achieved / peak,
+    peak = mma_peak if bound == "mma" else tf32_peak
+    out = {
+        "bound": "tensor", "unit": "TFLOP/s", "achieved": achieved, "peak": peak, "frac": achieved / peak,
         "traffic": (traffic or {}).get(top["name"]),
         "kernel": top["name"], "ms_per_launch": top["ms_per_launch"],
-        "work": "%.3f GFLOP per launch (algorithmic)" % (flop / 1e9),
-        "peak_source": ("fp32 FMA probe (bm_probe_fp32) measured in this run; MEASURED_PEAKS.json has no SIMT "
-                        "figure" if bound == "fp32" else
+        "work": "%.3f GFLOP of tf32 MMA per launch (3 x the fp32 algorithmic 2*256*C*E)" % (flop / 1e9)
+                if bound == "mma" else "%.3f GFLOP per launch (algorithmic)" % (flop / 1e9),
+        "peak_source": ("warp-level tf32 mma.sync probe (bm_probe_mma_tf32) measured in this run"
+                        if bound == "mma" else
                         "dense tf32 = MEASURED_PEAKS.json (%s) bf16 %.0f TF/s / 2" % (peak_kind,
                                                                                   peaks.get("bf16_tflops", 0))),
     }
+    if bound == "mma":
+        out["frac_of_dense_tf32"] = achieved / tf32_peak
+        out["dense_tf32_source"] = "MEASURED_PEAKS.json (%s) bf16 %.0f TF/s / 2" % (peak_kind,
+                                                                                 peaks.get("bf16_tflops", 0))
+    return out
 
 
 def kernel_table(nprof):
@@ -645,9 +673,9 @@ def run_sharded(args, world, rank, local):
     kernels = kernel_table(1)
     n_own = own.numel()
     n_local = n_own + sd.last_halo.n_from_left + sd.last_halo.n_from_right
-    fp32_peak = probe_fp32_tflops(lib)
+    mma_peak = probe_mma_tf32_tflops(lib)
     peaks, peak_kind = measured_peaks()
-    roofline = roofline_of(kernels, layer_work(e_local, n_own, n_local, cfg["c"]), fp32_peak,
+    roofline = roofline_of(kernels, layer_work(e_local, n_own, n_local, cfg["c"]), mma_peak,
                            peaks.get("bf16_tflops", 1590.0) / 2.0, peak_kind, peaks)
     roofline["stage_ms_rank0"] = stage_ms
     roofline["limiting_stage"] = max(stage_ms, key=stage_ms.get) if stage_ms else None
@@ -830,17 +858,19 @@ def main():
     lib.bm_profile_stop()
     kernels = kernel_table(nprof)
     n, c = CFG["n"], CFG["c"]
-    fp32_peak = probe_fp32_tflops(lib)
+    mma_peak = probe_mma_tf32_tflops(lib)
     peaks, peak_kind = measured_peaks()
     tf32_peak = peaks.get("bf16_tflops", 1590.0) / 2.0   # dense tf32 = half the bf16 rate
     # DRAM bytes (read + write) per launch from one ncu capture of each kernel at
-    # this workload (profiles/layer_kernels_config4_ncu_full.md gives the command)
+    # this workload (profiles/layer_edge_kernels_mma_config4_ncu.md and
+    # profiles/layer_kernels_config4_ncu_full.md give the commands)
     ncu_traffic = {
-        "layer_bwd(target)": 229.65e6 + 5.04e6,
-        "layer_fwd(aggregate)": 31.27e6 + 150.14e6,
+        "layer_bwd(target)": 230.76e6 + 4.98e6,
+        "layer_fwd(aggregate)": 31.34e6 + 148.60e6,
+        "layer_bwd(source aggregate)": 29.55e6 + 147.20e6,
         "tc_gemm(mix->irreps)": 213.12e6 + 20.42e6,
     }
-    roofline = roofline_of(kernels, layer_work(E, n, n, c), fp32_peak, tf32_peak, peak_kind, peaks, ncu_traffic)
+    roofline = roofline_of(kernels, layer_work(E, n, n, c), mma_peak, tf32_peak, peak_kind, peaks, ncu_traffic)
     roofline["traffic_unit"] = ("DRAM bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum of the "
                                 "capture in profiles/, same workload)")
     stage_ms = {k: v / 3 for k, v in stages.ms.items()}

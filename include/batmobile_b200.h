@@ -56,6 +56,11 @@ int64_t bm_launch_count(void);
  * (2 * 8 * iters FLOP per thread): a peak-fp32 probe for SIMT rooflines.
  * scratch: one device float (written only in a case that cannot occur). */
 int bm_probe_fp32(float* scratch, int iters, int blocks, void* stream);
+/* Measurement helper: the warp-level tf32 MMA rate of the device (mma.sync
+ * m16n8k8, 8 independent accumulators per warp, `blocks` CTAs of 256 threads,
+ * `iters` x 8 MMAs per warp), the denominator for the edge-sum and target passes.
+ * No reference counterpart (measurement only). */
+int bm_probe_mma_tf32(float* scratch, int iters, int blocks, void* stream);
 /* Precision of the per-path channel mixes, which run on the tensor cores:
  * 0 (default) = fp32-accurate (TF32 hi/lo split, three passes, ~1e-6 relative);
  * 1 = single-pass TF32 (~5e-4 relative; inside the 2e-3 tolerance allowed for a tf32 mix). */
