@@ -728,7 +728,8 @@ constexpr int kTMEpi = kTMCons + kTMProd;                    // first epilogue w
 constexpr int kTMThreads = 32 * (kTMCons + kTMProd + 2);     // two epilogue warps (one per batch parity)
 constexpr int kTMSlot = 4096 + 16;                           // x row slot (bytes): 4 mod 32 words
 constexpr int kTMdBPitch = 1028;                             // dB tile [m2][K] row pitch (floats)
-constexpr int kTMRedPitch = 20;                              // partials [warp][edge][m2 (+pad)]
+constexpr int kTMRedPitch = 20;
+constexpr int kTMMeta = 2 * kTBufs;                          // batches of edge metadata in flight                              // partials [warp][edge][m2 (+pad)]
 constexpr size_t kTMRingBytes = (size_t)kTBufs * kBatch * kTMSlot;
 constexpr size_t kTMdBBytes = (size_t)16 * kTMdBPitch * 4;
 constexpr size_t kTMRedBytes = (size_t)2 * kTMCons * kBatch * kTMRedPitch * 4;
@@ -805,16 +806,19 @@ layer_target_mma_kernel(const float* __restrict__ x, const float* __restrict__ d
   float* dSs = reinterpret_cast<float*>(tm_smem + kTMRingBytes);            // [156][64]
   float* dBt = reinterpret_cast<float*>(tm_smem + kTMRingBytes + kTdSBytes);  // [16][kTMdBPitch]
   float* red = reinterpret_cast<float*>(tm_smem + kTMRingBytes + kTdSBytes + kTMdBBytes);  // [2][16][8][20]
-  __shared__ TMeta meta[kTBufs * kBatch];
-  __shared__ uint64_t full[kTBufs], empty[kTBufs], dfull, dempty, red_full[2], red_empty[2];
+  // edge metadata lives in its own ring of 2 kTBufs batches, released by the
+  // epilogue (mempty), so an x-row buffer is free as soon as the consumers are done
+  __shared__ TMeta meta[kTMMeta * kBatch];
+  __shared__ uint64_t full[kTBufs], empty[kTBufs], mempty[kTMMeta], dfull, dempty, red_full[2], red_empty[2];
   __shared__ uint32_t turn;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   if (t == 0) {
     turn = 0;
     for (int i = 0; i < kTBufs; ++i) {
       tc::mbar_init(&full[i], 1);
-      tc::mbar_init(&empty[i], kTMCons + 1);  // consumers + epilogue
+      tc::mbar_init(&empty[i], kTMCons);
     }
+    for (int i = 0; i < kTMMeta; ++i) tc::mbar_init(&mempty[i], 1);
     tc::mbar_init(&dfull, 1);
     tc::mbar_init(&dempty, kTMCons);  // every consumer warp builds a part of dB
     for (int i = 0; i < 2; ++i) {
@@ -901,8 +905,10 @@ layer_target_mma_kernel(const float* __restrict__ x, const float* __restrict__ d
             const bool act = lane >= b0 && lane < b0 + cnt;
             const uint32_t buf = bi % kTBufs;
             LD_MARK()
+            const uint32_t mb = bi % kTMMeta;
             if (lane == 0) {
               if (b0 > 0 || g0 > eb) ok = wait_turn(&turn, bi, err);  // the first batch holds the turn already
+              if (ok && bi >= kTMMeta) ok = tc::mbar_wait(&mempty[mb], ((bi / kTMMeta) - 1) & 1, err);
               if (ok && bi >= kTBufs) ok = tc::mbar_wait(&empty[buf], ((bi / kTBufs) - 1) & 1, err);
             }
             LD_ADD(9)
@@ -911,7 +917,7 @@ layer_target_mma_kernel(const float* __restrict__ x, const float* __restrict__ d
             const uint32_t mine = (act && srow >= 0) ? row_bytes : 0u;
             if (act) {
               const int sl = buf * kBatch + (lane - b0);
-              meta[sl] = m;
+              meta[mb * kBatch + (lane - b0)] = m;
               if (srow >= 0) tc::bulk_g2s(ring + (size_t)sl * kTMSlot, x + srow * (int64_t)Ci * 16, row_bytes, &full[buf]);
             }
             const uint32_t total = __reduce_add_sync(0xffffffffu, mine);
@@ -941,7 +947,7 @@ layer_target_mma_kernel(const float* __restrict__ x, const float* __restrict__ d
       const int64_t eb = row_ptr[n], ee = row_ptr[n + 1];
       for (int64_t e0 = eb; e0 < ee && ok; e0 += kBatch, ++bi) {
         const int cnt = (int)imin64(kBatch, ee - e0);
-        const uint32_t buf = bi % kTBufs, par = bi & 1;
+        const uint32_t par = bi & 1;
         if (par != mine) continue;
         LD_MARK()
         if (!tc::mbar_wait(&red_full[par], (bi >> 1) & 1, err)) { ok = false; break; }
@@ -963,7 +969,7 @@ layer_target_mma_kernel(const float* __restrict__ x, const float* __restrict__ d
           dyv[4 * k + 3] = __shfl_sync(0xffffffffu, dq.w, srcl);
         }
         if (mq == 0 && je < cnt) {
-          const TMeta mm = meta[buf * kBatch + je];
+          const TMeta mm = meta[(bi % kTMMeta) * kBatch + je];
           if (!mm.valid) {  // the ring slot of an invalid source holds stale rows
 #pragma unroll
             for (int m2 = 0; m2 < 16; ++m2) dyv[m2] = 0.0f;
@@ -974,7 +980,7 @@ layer_target_mma_kernel(const float* __restrict__ x, const float* __restrict__ d
         LD_ADD(12)
         if (lane == 0) {
           tc::mbar_arrive(&red_empty[par]);
-          tc::mbar_arrive(&empty[buf]);
+          tc::mbar_arrive(&mempty[bi % kTMMeta]);
         }
       }
     }
