@@ -767,7 +767,7 @@ __device__ __forceinline__ void dB_quarter_half(const float* __restrict__ dSs, i
     float& r_ = ((j) & 1) ? d[m1][(j) >> 1].y : d[m1][(j) >> 1].x;              \
     r_ = fmaf((coeff), col[(slot) * 64], r_);                                   \
   }
-#define BM_F() asm volatile("" ::: "memory");
+#define BM_F()
   if constexpr (Q == 0) { BM_CG_M2Q_0(BM_X, BM_F) }
   if constexpr (Q == 1) { BM_CG_M2Q_1(BM_X, BM_F) }
   if constexpr (Q == 2) { BM_CG_M2Q_2(BM_X, BM_F) }
@@ -959,6 +959,9 @@ layer_target_mma_kernel(const float* __restrict__ x, const float* __restrict__ d
           const float4 r4 = *reinterpret_cast<const float4*>(rp + w * kBatch * kTMRedPitch);
           dq.x += r4.x; dq.y += r4.y; dq.z += r4.z; dq.w += r4.w;
         }
+        // the partials are in registers: hand the buffer back before the chain rule
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&red_empty[par]);
         float dyv[16];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -978,10 +981,7 @@ layer_target_mma_kernel(const float* __restrict__ x, const float* __restrict__ d
         }
         __syncwarp();
         LD_ADD(12)
-        if (lane == 0) {
-          tc::mbar_arrive(&red_empty[par]);
-          tc::mbar_arrive(&mempty[bi % kTMMeta]);
-        }
+        if (lane == 0) tc::mbar_arrive(&mempty[bi % kTMMeta]);
       }
     }
     LD_FLUSH(13)
