@@ -185,9 +185,17 @@ class GraphedStep:
     gradient); the kernels walk the CSR offsets the replay computed, so only the
     first E slots of the buffers are touched.  A list longer than the capacity
     sets the device error flag (the fill drops what does not fit); `check()`
-    reads it and `edges()` reads E, both outside the timed region."""
+    reads it and `edges()` reads E, both outside the timed region.
 
-    def __init__(self, bm, _bm, lib, cfg, pos, x, W, G, headroom=0.125):
+    With `host` (pinned host tensors out, gx, gw, gpos) a third graph is captured
+    for the end-to-end step: the same kernels, with the results copied to the
+    host on a copy stream as soon as each is final (the layer output during the
+    backward, the feature gradient during the edge-gradient pass), instead of
+    after the step.  The backward runs as two API calls for that (feature
+    gradient first, then edge and weight gradients); the device-resident graph
+    uses the same split."""
+
+    def __init__(self, bm, _bm, lib, cfg, pos, x, W, G, headroom=0.125, host=None):
         self.bm, self._bm, self.lib, self.cfg = bm, _bm, lib, cfg
         self.pos, self.x, self.W, self.G = pos, x, W, G
         self.plan = _bm.NeighborListPlan(pos, [cfg["box"]] * 3, cfg["rc"])
@@ -201,9 +209,16 @@ class GraphedStep:
         self.graph_a = self._capture(self._edges)
         self.graph = self._out
         self.launches = self._captured_launches
+        self.host = None
         self.graph_b = self._capture(self._layer)
         self.launches += self._captured_launches
         self.outputs = self._out
+        self.graph_e2e = None
+        if host is not None:
+            self.host = host
+            self.copy = torch.cuda.Stream(device=dev)
+            self.graph_e2e = self._capture(self._layer)
+            self.outputs_e2e = self._out
 
     def _capture(self, fn):
         side = torch.cuda.Stream()
@@ -227,21 +242,40 @@ class GraphedStep:
         graph.src_csr  # builds the source-grouped view inside this graph
         return graph
 
+    def _to_host(self, name, t):
+        if self.host is None:
+            return
+        self.copy.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(self.copy):
+            self.host[name].copy_(t, non_blocking=True)
+
     def _layer(self):
         _bm, graph = self._bm, self.graph
         out, slots = _bm.layer_forward(self.x, self.vec, self.W, graph.src, graph.row_ptr_dst, graph.perm_dst)
+        self._to_host("out", out)
         rps, ps = graph.src_csr
-        gx, gv, gw = _bm.layer_backward(self.x, self.vec, self.W, graph.src, graph.dst, graph.row_ptr_dst,
-                                        graph.perm_dst, rps, ps, slots, self.G)
+        args = (self.x, self.vec, self.W, graph.src, graph.dst, graph.row_ptr_dst, graph.perm_dst, rps, ps,
+                slots, self.G)
+        gx, _, _ = _bm.layer_backward(*args, needs_x=True, needs_v=False, needs_w=False)
+        self._to_host("gx", gx)
+        _, gv, gw = _bm.layer_backward(*args, needs_x=False, needs_v=True, needs_w=True)
         gpos = _bm.edge_grad_to_pos(gv, graph.row_ptr_dst, graph.perm_dst, rps, ps)
+        self._to_host("gw", gw)
+        self._to_host("gpos", gpos)
+        if self.host is not None:
+            torch.cuda.current_stream().wait_stream(self.copy)
         return out, gx, gw, gpos
 
-    def __call__(self, x_ready=None):
+    def __call__(self, x_ready=None, e2e=False):
         self.graph_a.replay()
         if x_ready is not None:  # node features copied in on a side stream meanwhile
             torch.cuda.current_stream().wait_event(x_ready)
-        self.graph_b.replay()
-        out, gx, gw, gpos = self.outputs
+        if e2e:  # results land in the pinned host tensors given at construction
+            self.graph_e2e.replay()
+            out, gx, gw, gpos = self.outputs_e2e
+        else:
+            self.graph_b.replay()
+            out, gx, gw, gpos = self.outputs
         return out, gx, gw, gpos, self.E
 
     def edges(self):
@@ -769,7 +803,12 @@ def main():
     pos, x, W, G = (t.to(dev) for t in (pos_h, x_h, W_h, G_h))
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)  # > L2 (126 MB)
 
-    step = GraphedStep(bm, _bm, lib, CFG, pos, x, W, G)
+    # pinned host buffers of the end-to-end step (its graph copies the results into them)
+    pin = lambda t: t.pin_memory()  # noqa: E731
+    pos_p, x_p = pin(pos_h), pin(x_h)
+    host = {"gpos": torch.empty(CFG["n"], 3).pin_memory(), "gw": torch.empty_like(W_h).pin_memory(),
+            "out": torch.empty(CFG["n"], CFG["c"], 16).pin_memory(), "gx": torch.empty_like(x_h).pin_memory()}
+    step = GraphedStep(bm, _bm, lib, CFG, pos, x, W, G, host=host)
     clk = ClockSampler(local).__enter__()  # spans warm-up and the timed region
     clk.wait_first()
     for _ in range(args.warmup):
@@ -808,15 +847,10 @@ def main():
     t_step = max_over_ranks(sum(step_ms) / len(step_ms), world)
     value = world * E / (t_step * 1e-3) / 1e6
 
-    # ---- end to end through the public API: host inputs -> device -> host results
-    pin = lambda t: t.pin_memory()  # noqa: E731
-    pos_p, x_p = pin(pos_h), pin(x_h)
-    gpos_p = torch.empty(CFG["n"], 3).pin_memory()
-    gw_p = torch.empty_like(W_h).pin_memory()
-    out_p = torch.empty(CFG["n"], CFG["c"], 16).pin_memory()
-    gx_p = torch.empty_like(x_h).pin_memory()
+    # ---- end to end through the public API: host inputs -> device -> host results;
+    # the results go back on a copy stream as soon as each is final (inside the graph)
     h2d = pos_p.numel() * 4 + x_p.numel() * 4
-    d2h = (gpos_p.numel() + gw_p.numel() + out_p.numel() + gx_p.numel()) * 4
+    d2h = sum(t.numel() for t in host.values()) * 4
     e2e_ms = []
     copy_stream = torch.cuda.Stream(device=dev)
     main = torch.cuda.current_stream()
@@ -833,11 +867,7 @@ def main():
         with torch.cuda.stream(copy_stream):
             x.copy_(x_p, non_blocking=True)
             x_ready.record()
-        out_d, gx_d, gw_d, gpos_d, _ = step(x_ready=x_ready)
-        gpos_p.copy_(gpos_d, non_blocking=True)
-        gw_p.copy_(gw_d, non_blocking=True)
-        out_p.copy_(out_d, non_blocking=True)
-        gx_p.copy_(gx_d, non_blocking=True)
+        step(x_ready=x_ready, e2e=True)
         e.record()
         e.synchronize()
         if i >= args.warmup:
@@ -935,7 +965,8 @@ def main():
                         "ms_per_step_min_max": [min(e2e_ms), max(e2e_ms)],
                         "what": "pinned host positions + node features in (features on a copy stream, overlapping "
                                 "the neighbour list); layer output, feature gradients, forces and weight gradients "
-                                "out"},
+                                "out on a copy stream as each is final (the output during the backward, the "
+                                "feature gradient during the edge-gradient pass)"},
                 "gpu_launches": launches // args.steps * args.steps,
                 "gpu_launches_per_step": launches / args.steps,
                 "roofline": roofline, "kernels": kernels, "mace_step": mace, "tf32_mix": tf32_mix,

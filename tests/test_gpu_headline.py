@@ -40,7 +40,9 @@ def test_graphed_step_at_benchmark_size_matches_oracle(bm, oracle, bench_mod):
     n = cfg["n"]
     pos_h, x_h, W_h, G_h = bench_mod.make_inputs(cfg)
     pos, x, W, G = (t.to(dev) for t in (pos_h, x_h, W_h, G_h))
-    step = bench_mod.GraphedStep(bm, _bm, lib, cfg, pos, x, W, G)
+    host = {"gpos": torch.empty(n, 3).pin_memory(), "gw": torch.empty_like(W_h).pin_memory(),
+            "out": torch.empty(n, cfg["c"], 16).pin_memory(), "gx": torch.empty_like(x_h).pin_memory()}
+    step = bench_mod.GraphedStep(bm, _bm, lib, cfg, pos, x, W, G, host=host)
     out, gx, gw, gpos, E = (t.clone() if torch.is_tensor(t) else t for t in step())
     # a second replay with the features copied in from pinned memory on a side
     # stream (the end-to-end path) gives the same bits
@@ -56,6 +58,13 @@ def test_graphed_step_at_benchmark_size_matches_oracle(bm, oracle, bench_mod):
     assert E2 == E
     for a, b in ((out, out2), (gx, gx2), (gw, gw2), (gpos, gpos2)):
         assert torch.equal(a, b)
+    # the end-to-end graph: the same kernels, results streamed into pinned host memory
+    for t in host.values():
+        t.fill_(float("nan"))
+    step(x_ready=None, e2e=True)
+    torch.cuda.synchronize()
+    for a, k in ((out, "out"), (gx, "gx"), (gw, "gw"), (gpos, "gpos")):
+        assert torch.equal(a.cpu(), host[k])
 
     step.check()   # the list fitted the step's edge buffers, no device wait timed out
     rei, rvec = oracle.nl_cells(pos_h, [cfg["box"]] * 3, cfg["rc"])
