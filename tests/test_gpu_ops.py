@@ -96,6 +96,47 @@ def test_tp_simple_forward_backward(bm, oracle):
     assert relerr(ga, ra) < TOL and relerr(gb, rb) < TOL
 
 
+def _unaligned(t):
+    """The same values at an address 4 bytes past a 16-byte boundary."""
+    flat = torch.empty(t.numel() + 1, device=t.device, dtype=t.dtype)
+    flat[1:] = t.reshape(-1)
+    return flat[1:].view(t.shape)
+
+
+@pytest.mark.parametrize("E", [1, 3, 127, 128, 129, 1000, 300001])
+def test_streaming_tile_edges(bm, oracle, E):
+    """The persistent TMA-staged L = 3 kernels at ragged tile ends (128-edge
+    tiles, several tiles per CTA at the larger sizes): SH forward and backward
+    equal the per-block kernels (taken for unaligned inputs) bit for bit; the
+    simple tensor product matches the oracle."""
+    g = torch.Generator().manual_seed(E)
+    v = unit(E, E).to(dev)
+    Y = bm.spherical_harmonics(v, 3)
+    assert torch.equal(Y, bm.spherical_harmonics(_unaligned(v), 3))
+    gY = torch.randn(E, 16, generator=g).to(dev)
+    gv = bm.spherical_harmonics_backward(v, gY)
+    assert torch.equal(gv, bm.spherical_harmonics_backward(_unaligned(v), gY))
+    if E <= 1000:
+        assert relerr(Y, oracle.sh(v.double().cpu(), 3)) < TOL
+        assert relerr(gv, oracle.sh_backward(v.double().cpu(), gY.double().cpu())) < TOL
+    a, b, go = (torch.randn(E, 16, generator=g) for _ in range(3))
+    out = bm.tensor_product_simple(a.to(dev), b.to(dev))
+    assert relerr(out, oracle.tp_simple(a.double(), b.double())) < TOL
+    ga, gb = bm.tensor_product_simple_backward(a.to(dev), b.to(dev), go.to(dev))
+    if E <= 1000:
+        ra, rb = oracle.grads(oracle.tp_simple, [a.double(), b.double()], go.double())
+        assert relerr(ga, ra) < TOL and relerr(gb, rb) < TOL
+    else:   # linearity of each gradient in the upstream gradient and the other operand
+        ga2, _ = bm.tensor_product_simple_backward(a.to(dev), b.to(dev), (2 * go).to(dev))
+        assert torch.equal(ga2, 2 * ga)
+        _, gb_ = bm.tensor_product_simple_backward(a.to(dev), b.to(dev), go.to(dev))
+        assert torch.equal(gb_, gb)
+        ref_gb = oracle.grads(oracle.tp_simple, [a[:2000].double(), b[:2000].double()], go[:2000].double())[1]
+        assert relerr(gb[:2000], ref_gb) < TOL
+        ref_ga = oracle.grads(oracle.tp_simple, [a[-2000:].double(), b[-2000:].double()], go[-2000:].double())[0]
+        assert relerr(ga[-2000:], ref_ga) < TOL
+
+
 @pytest.mark.parametrize("n,ci,co", [(1000, 32, 64), (257, 8, 16), (33, 5, 7)])
 def test_tp_weighted_forward_backward(bm, oracle, n, ci, co):
     # the 1000-atom C_in=32, C_out=64 benchmark shape first; odd channel counts exercise the tile edges
