@@ -203,35 +203,44 @@ __global__ void nl_scatter_kernel(const float* __restrict__ pos, int64_t N, cons
 // Candidate ranges of the 27 cells around cell c in the cell-sorted atom order:
 // the three cells x-1, x, x+1 of each of the 9 (y, z) rows are adjacent in that
 // order, so a row is one contiguous range, or two where it wraps around the
-// periodic x boundary (x = 0 or x = nb-1).  f(begin, end) per range.
-template <class F>
-__device__ __forceinline__ void for_neighbor_ranges(int c, const NLGeom& g, const int64_t* __restrict__ cell_start,
-                                                    F&& f) {
+// periodic x boundary (x = 0 or x = nb-1).  Lane r < 18 gets part r & 1 of
+// row r >> 1 as [b, e) (empty where the row needs one range only, and for
+// lanes 18..31).
+__device__ __forceinline__ void lane_range(int c, const NLGeom& g, const int64_t* __restrict__ cell_start, int lane,
+                                           int64_t& b, int64_t& e) {
+  b = e = 0;
+  if (lane >= 18) return;
   const int nx = g.nb[0];
   const int cx = c % nx;
   const int cy = (c / nx) % g.nb[1];
   const int cz = c / (nx * g.nb[1]);
-  for (int dz = -1; dz <= 1; ++dz) {
-    int z = cz + dz; z += (z < 0) ? g.nb[2] : 0; z -= (z >= g.nb[2]) ? g.nb[2] : 0;
-    for (int dy = -1; dy <= 1; ++dy) {
-      int y = cy + dy; y += (y < 0) ? g.nb[1] : 0; y -= (y >= g.nb[1]) ? g.nb[1] : 0;
-      const int row = (z * g.nb[1] + y) * nx;
-      if (cx == 0) {                       // cells nx-1 | 0, 1
-        f(cell_start[row], cell_start[row + 2]);
-        f(cell_start[row + nx - 1], cell_start[row + nx]);
-      } else if (cx == nx - 1) {           // cells nx-2, nx-1 | 0
-        f(cell_start[row + nx - 2], cell_start[row + nx]);
-        f(cell_start[row], cell_start[row + 1]);
-      } else {
-        f(cell_start[row + cx - 1], cell_start[row + cx + 2]);
-      }
-    }
+  const int rw = lane >> 1, part = lane & 1;
+  int z = cz + rw / 3 - 1; z += (z < 0) ? g.nb[2] : 0; z -= (z >= g.nb[2]) ? g.nb[2] : 0;
+  int y = cy + rw % 3 - 1; y += (y < 0) ? g.nb[1] : 0; y -= (y >= g.nb[1]) ? g.nb[1] : 0;
+  const int row = (z * g.nb[1] + y) * nx;
+  int c0, c1;   // cells [c0, c1) of this part
+  if (cx == 0) {                 // cells nx-1 | 0, 1
+    c0 = part ? row + nx - 1 : row;
+    c1 = part ? row + nx : row + 2;
+  } else if (cx == nx - 1) {     // cells nx-2, nx-1 | 0
+    c0 = part ? row : row + nx - 2;
+    c1 = part ? row + 1 : row + nx;
+  } else {
+    if (part) return;
+    c0 = row + cx - 1;
+    c1 = row + cx + 2;
   }
+  b = cell_start[c0];
+  e = cell_start[c1];
 }
 
-// One warp per atom (atoms in cell order for locality): the lanes stride over
-// the candidates of each contiguous range of the 27 surrounding cells; matches are counted with ballots and,
-// in the write pass, compacted to ballot-prefix positions (the row is sorted
+// One warp per atom (atoms in cell order for locality).  The candidates of
+// the up to 18 ranges are numbered 0..T-1 in range order; pass p hands
+// candidate 32p + lane to each lane (range found by a binary search over the
+// lanes' running totals), and the next pass's loads are issued before this
+// pass's distance checks, so a row costs about one memory latency per pass
+// rather than two per range.  Matches are counted with ballots and, in the
+// write pass, compacted to ballot-prefix positions (the row is sorted
 // afterwards, so the order here is irrelevant).
 template <bool kWrite, class IdxT>
 __global__ void __launch_bounds__(128) nl_pairs_kernel(int64_t N, NLGeom g, bool self_loops,
@@ -241,6 +250,7 @@ __global__ void __launch_bounds__(128) nl_pairs_kernel(int64_t N, NLGeom g, bool
                                                        const float4* __restrict__ sorted_pos,
                                                        int* __restrict__ cnt, const int64_t* __restrict__ row_ptr,
                                                        IdxT* __restrict__ tmp_j, int64_t E, int* __restrict__ err) {
+  const unsigned full = 0xffffffffu;
   const int lane = threadIdx.x & 31;
   const int64_t k = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (k >= N) return;
@@ -250,27 +260,55 @@ __global__ void __launch_bounds__(128) nl_pairs_kernel(int64_t N, NLGeom g, bool
     return;
   }
   const float4 pi = sorted_pos[k];
+  int64_t rb, re;
+  lane_range(cell_of[i], g, cell_start, lane, rb, re);
+  const int len = (int)(re - rb);
+  int incl = len;   // inclusive running total over the lanes
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int t = __shfl_up_sync(full, incl, d);
+    if (lane >= d) incl += t;
+  }
+  const int total = __shfl_sync(full, incl, 31);
+  const int64_t off = rb - (int64_t)(incl - len);   // candidate number t of range r is atom rb_r + t - excl_r
+  // the atom a lane checks in the pass starting at `base` (q < 0: none)
+  auto locate = [&](int base) -> int64_t {
+    const int kk = base + lane;
+    int lo = 0;
+#pragma unroll
+    for (int step = 16; step >= 1; step >>= 1) {
+      const int v = __shfl_sync(full, incl, lo + step - 1);
+      if (v <= kk) lo += step;
+    }
+    const int64_t o = __shfl_sync(full, off, lo);
+    return kk < total ? o + kk : -1;
+  };
   int64_t w = kWrite ? row_ptr[i] : 0;
   int count = 0;
-  for_neighbor_ranges(cell_of[i], g, cell_start, [&](int64_t b, int64_t e) {
-    for (int64_t q0 = b; q0 < e; q0 += 32) {
-      const int64_t q = q0 + lane;
-      bool hit = false;
-      int j = -1;
-      if (q < e) {
-        j = sorted_idx[q];
-        hit = (j != i || self_loops) && pair_within(pi, sorted_pos[q], g);
-      }
-      const unsigned m = __ballot_sync(0xffffffffu, hit);
-      if (kWrite && hit) {
-        const int64_t o = w + __popc(m & ((1u << lane) - 1u));
-        if (o < E) tmp_j[o] = (IdxT)j;
-        else atomicOr(err, 4);  // buffers shorter than the counted list: drop, flag
-      }
-      w += __popc(m);
-      count += __popc(m);
+  int64_t qn = locate(0);
+  int jn = -1;
+  float4 pn = pi;
+  if (qn >= 0) { jn = sorted_idx[qn]; pn = sorted_pos[qn]; }
+  for (int base = 0; base < total; base += 32) {
+    const int j = jn;
+    const float4 pj = pn;
+    const bool valid = qn >= 0;
+    if (base + 32 < total) {   // warp-uniform
+      qn = locate(base + 32);
+      if (qn >= 0) { jn = sorted_idx[qn]; pn = sorted_pos[qn]; }
+    } else {
+      qn = -1;
     }
-  });
+    const bool hit = valid && (j != i || self_loops) && pair_within(pi, pj, g);
+    const unsigned m = __ballot_sync(full, hit);
+    if (kWrite && hit) {
+      const int64_t o = w + __popc(m & ((1u << lane) - 1u));
+      if (o < E) tmp_j[o] = (IdxT)j;
+      else atomicOr(err, 4);  // buffers shorter than the counted list: drop, flag
+    }
+    w += __popc(m);
+    count += __popc(m);
+  }
   if (!kWrite && lane == 0) cnt[i] = count;
 }
 
