@@ -202,6 +202,12 @@ constexpr int kSplitWarps = 4, kEpi = 128;
 constexpr int kWsThreads = 32 + 32 * kSplitWarps + 32 + kEpi;
 constexpr int kMmaWarp = 1 + kSplitWarps;
 constexpr int kMaxStages = 8;
+#ifndef BM_GEMM_AHI_TMEM
+#define BM_GEMM_AHI_TMEM 0
+#endif
+// TMEM columns per stage for the split A operand: lo only (hi = the raw slab
+// in shared memory, which kind::tf32 reads as tf32), or hi and lo.
+constexpr int kALoCols = BM_GEMM_AHI_TMEM ? 64 : 32;
 
 template <int BN, bool kSplit3, bool kTmaStore = false>
 struct Smem {
@@ -218,8 +224,9 @@ struct Smem {
   // an accumulator is 2 BN columns wide; the epilogue adds the two halves.
   static constexpr bool kFuse = kSplit3 && BN == 64;
   static constexpr int kAccCols = kFuse ? 2 * BN : BN;
-  // kSplit3: TMEM holds 2 accumulators + per stage A hi and lo (64 columns)
-  static constexpr int kTmemFit = kSplit3 ? (512 - 2 * kAccCols) / 64 : kMaxStages;
+  // kSplit3: TMEM holds 2 accumulators + per stage the A lo part (32 columns;
+  // the A hi products read the raw slab from shared memory)
+  static constexpr int kTmemFit = kSplit3 ? (512 - 2 * kAccCols) / kALoCols : kMaxStages;
   static constexpr int kFit2 = kFit < kTmemFit ? kFit : kTmemFit;
   static constexpr int kStages = kFit2 > kMaxStages ? kMaxStages : kFit2;
   static constexpr int kBytes = kStages * kStage + kEpiStage + 1024;  // + alignment slack
@@ -461,11 +468,17 @@ __global__ void __launch_bounds__(kWsThreads, 1) tc_gemm_kernel(const __grid_con
           const uint8_t* st = smem + s * L::kStage;
           float v[32];
           load_a_row<P::kAMN>(st, row, v);
-          const uint32_t ta = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(2 * L::kAccCols + s * 64);
+          const uint32_t ta = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(2 * L::kAccCols + s * kALoCols);
+#if BM_GEMM_AHI_TMEM
           tmem_st32(ta, v);
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = tf32_lo(v[j]);
           tmem_st32(ta + 32, v);
+#else
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = tf32_lo(v[j]);
+          tmem_st32(ta, v);
+#endif
           uint8_t* sb = smem + s * L::kStage + L::kA;
 #pragma unroll 4
           for (int o = st_t * 16; o < L::kB; o += 32 * kSplitWarps * 16) {
@@ -504,20 +517,36 @@ __global__ void __launch_bounds__(kWsThreads, 1) tc_gemm_kernel(const __grid_con
         tc_fence_after();
         if (lane == 0 && ok) {
           const uint32_t a_sm = sbase + s * L::kStage, b_hi = a_sm + L::kA, b_lo = b_hi + L::kB;
-          const uint32_t a_tm = tmem + (uint32_t)(2 * L::kAccCols + s * 64);  // A hi; lo 32 columns on
+          const uint32_t a_tm = tmem + (uint32_t)(2 * L::kAccCols + s * kALoCols);
+          constexpr uint32_t kLo = BM_GEMM_AHI_TMEM ? 32 : 0;   // A lo column offset in the stage
 #pragma unroll
           for (int kk = 0; kk < kBK / 8; ++kk) {
             const uint64_t bd = op_desc<BN, P::kBMN>(b_hi, kk);
+#if BM_GEMM_AHI_TMEM
             if constexpr (L::kFuse) {
               // B lo sits right after B hi: one N = 2 BN operand [B_hi | B_lo]
               constexpr uint32_t idesc_f = idesc_tf32(kBM, 2 * BN, 0, P::kBMN ? 1 : 0);
               mma_tf32_ta(dacc, a_tm + kk * 8, bd, idesc_f, (kb > 0 || kk > 0) ? 1u : 0u);
-              mma_tf32_ta(dacc + BN, a_tm + 32 + kk * 8, bd, idesc_t, 1u);
+              mma_tf32_ta(dacc + BN, a_tm + kLo + kk * 8, bd, idesc_t, 1u);
             } else if (kSplit3) {
               mma_tf32_ta(dacc, a_tm + kk * 8, bd, idesc_t, (kb > 0 || kk > 0) ? 1u : 0u);
               mma_tf32_ta(dacc, a_tm + kk * 8, op_desc<BN, P::kBMN>(b_lo, kk), idesc_t, 1u);
-              mma_tf32_ta(dacc, a_tm + 32 + kk * 8, bd, idesc_t, 1u);
+              mma_tf32_ta(dacc, a_tm + kLo + kk * 8, bd, idesc_t, 1u);
             } else {
+#else
+            if constexpr (L::kFuse) {
+              // B lo sits right after B hi: one N = 2 BN operand [B_hi | B_lo], A hi
+              // straight from the staged slab
+              constexpr uint32_t idesc_f = idesc_tf32(kBM, 2 * BN, P::kAMN ? 1 : 0, P::kBMN ? 1 : 0);
+              mma_tf32(dacc, op_desc<kBM, P::kAMN>(a_sm, kk), bd, idesc_f, (kb > 0 || kk > 0) ? 1u : 0u);
+              mma_tf32_ta(dacc + BN, a_tm + kLo + kk * 8, bd, idesc_t, 1u);
+            } else if (kSplit3) {
+              const uint64_t ad = op_desc<kBM, P::kAMN>(a_sm, kk);
+              mma_tf32(dacc, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+              mma_tf32(dacc, ad, op_desc<BN, P::kBMN>(b_lo, kk), idesc, 1u);
+              mma_tf32_ta(dacc, a_tm + kLo + kk * 8, bd, idesc_t, 1u);
+            } else {
+#endif
               mma_tf32(dacc, op_desc<kBM, P::kAMN>(a_sm, kk), bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
             }
           }
