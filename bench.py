@@ -782,6 +782,35 @@ def run_sharded(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def trace_step(step, replays):
+    """Kernel timeline of `replays` warm replays of the graphed step from a
+    CUPTI trace (torch.profiler): per-kernel device time per replay, and for
+    the last replay its span from the first kernel's start to the last one's
+    end against the kernels' summed durations (the difference is idle time)."""
+    from torch.profiler import profile, ProfilerActivity
+    for _ in range(5):
+        step()
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(replays):
+            step()
+        torch.cuda.synchronize()
+    evs = sorted((e for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA),
+                 key=lambda e: e.time_range.start)
+    per = {}
+    for e in evs:
+        k = e.name.split("(")[0]
+        per[k] = per.get(k, 0.0) + (e.time_range.end - e.time_range.start) / replays
+    firsts = [i for i, e in enumerate(evs) if "nl_bin_kernel" in e.name]
+    last = evs[firsts[-1]:] if firsts else evs
+    span = last[-1].time_range.end - last[0].time_range.start if last else 0.0
+    busy = sum(e.time_range.end - e.time_range.start for e in last)
+    print(json.dumps({"trace": "graphed 5000-atom step, %d warm replays" % replays,
+                      "us_per_replay": dict(sorted(per.items(), key=lambda kv: -kv[1])),
+                      "last_replay_span_us": span, "last_replay_kernels_us": busy,
+                      "idle_us": span - busy}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -789,6 +818,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--trace", action="store_true",
+                    help="5000-atom step: CUPTI kernel timeline of warm graph replays (torch.profiler), "
+                         "per-kernel device time per replay and the idle time between kernels; no bench line")
     ap.add_argument("--config", type=int, default=None, choices=[2, 3, 4, 5],
                     help="4 = single-GPU layer step (default at 1 GPU); 5 = 1M-atom sharded step (default at >1 GPU); "
                          "2 / 3 = the standalone-op workloads (SH + TP simple on 1M edges; weighted TP)")
@@ -820,6 +852,9 @@ def main():
     dev = torch.device("cuda", local)
     pos_h, x_h, W_h, G_h = make_inputs(CFG)
     pos, x, W, G = (t.to(dev) for t in (pos_h, x_h, W_h, G_h))
+    if args.trace:
+        trace_step(GraphedStep(bm, _bm, lib, CFG, pos, x, W, G), max(args.steps, 1))
+        return
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)  # > L2 (126 MB)
 
     # pinned host buffers of the end-to-end step (its graph copies the results into them)
