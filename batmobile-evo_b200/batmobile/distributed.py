@@ -15,12 +15,13 @@ Communication goes through torch.distributed point-to-point batches (NCCL over
 NVLink on B200s, gloo on the CPU in tests).  Per step:
   1. a header exchange with both neighbours: (magic, step id, ghost count);
      the one host read of the exchange (the counts size the receive buffers);
-  2. ghost positions (checked on arrival), then the ghost features, posted
-     without a host wait: the feature transfer overlaps the neighbour list
-     and the CSR build;
+  2. ghost positions, then the ghost features, both posted before the host
+     waits for the positions (checked on arrival); the feature transfer
+     overlaps the neighbour list and the CSR build;
   3. after the backward, one batch returns the ghosts' feature and position
-     gradients (reverse halo) while the weight-gradient all-reduce runs
-     asynchronously beside it.
+     gradients (reverse halo, sent as contiguous row ranges) while the
+     weight-gradient all-reduce runs beside it; the compute stream waits for
+     the all-reduce only after the reverse halo is posted.
 Failure handling: every host-side wait polls the outstanding work against a
 deadline (`timeout` seconds).  When it runs out -- a peer that died or never
 sends, a truncated or mismatched message -- the process group is aborted
@@ -195,8 +196,18 @@ class SlabDecomposition:
     def _pack(self, a: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
         """Rows a[idx] followed by the trailer row (magic, step id, count)."""
         n = idx.numel()
-        buf = a.new_zeros((n + 1,) + tuple(a.shape[1:]))
+        buf = a.new_empty((n + 1,) + tuple(a.shape[1:]))
         torch.index_select(a, 0, idx, out=buf[:n])
+        return self._trail(buf, n)
+
+    def _pack_range(self, a: torch.Tensor, start: int, n: int) -> torch.Tensor:
+        """Rows a[start:start + n] followed by the trailer row."""
+        buf = a.new_empty((n + 1,) + tuple(a.shape[1:]))
+        buf[:n].copy_(a[start:start + n])
+        return self._trail(buf, n)
+
+    def _trail(self, buf: torch.Tensor, n: int) -> torch.Tensor:
+        buf[n].zero_()
         tr = buf[n].reshape(-1)
         for k, val in enumerate((_MAGIC_F, float(self.step_id), float(n))):
             tr[k].fill_(val)   # device-side fills, no host synchronisation
@@ -263,18 +274,19 @@ class SlabDecomposition:
             out.append(torch.cat([fl, fr], 0))
         return out
 
-    def scatter_ghost_grads(self, h: Halo, grads_owned, grads_ghost):
+    def scatter_ghost_grads(self, h: Halo, grads_owned, grads_ghost, mark=lambda name: None):
         """Reverse halo of several arrays in one batch: each ghost gradient goes
         back to its owner and is added to the owner's row (fixed order: the
         returns from the left neighbour, then the right's).  Returns the
-        summed owned gradients."""
+        summed owned gradients.  `mark` records stage boundaries (packing,
+        transfer, sum)."""
         if self.world == 1:
             return list(grads_owned)
         ops, rets = [], []
         for gown, gg in zip(grads_owned, grads_ghost):
             nl, nr = h.n_from_left, h.n_from_right
-            gl = self._pack(gg, torch.arange(nl, device=gg.device))
-            gr = self._pack(gg, torch.arange(nl, nl + nr, device=gg.device))
+            gl = self._pack_range(gg, 0, nl)
+            gr = self._pack_range(gg, nl, nr)
             shape = tuple(gg.shape[1:])
             ns_l, ns_r = h.send_left.numel(), h.send_right.numel()
             ret_right = torch.empty((ns_r + 1,) + shape, dtype=gg.dtype, device=gg.device)
@@ -286,11 +298,13 @@ class SlabDecomposition:
             self._trailers += [(ret_right[ns_r], ns_r, "reverse halo", self.right),
                                (ret_left[ns_l], ns_l, "reverse halo", self.left)]
             rets.append((ret_left[:ns_l], ret_right[:ns_r]))
+        mark("reverse_pack")
         works = dist.batch_isend_irecv(ops)
         if grads_owned[0].is_cuda:
             self._stream_wait(works, "reverse halo")
         else:
             self._deadline_wait(works, "reverse halo")
+        mark("reverse_transfer")
         out = []
         for gown, (ret_left, ret_right) in zip(grads_owned, rets):
             gown.index_add_(0, h.send_left, ret_left)    # in place: the owned rows of the step's own gradient
@@ -298,14 +312,17 @@ class SlabDecomposition:
             out.append(gown)
         return out
 
-    def allreduce_sum(self, t: torch.Tensor, block: bool = True) -> torch.Tensor:
+    def allreduce_sum(self, t: torch.Tensor, block: bool = True):
+        """Sums t over the ranks in place.  block=False on device tensors posts
+        the all-reduce and returns (t, works) for `_stream_wait` later, so
+        that the current stream is not held behind it meanwhile."""
         if self.world > 1:
             w = dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
             if block or not t.is_cuda:
                 self._deadline_wait([w], "weight-gradient all-reduce")
             else:
-                self._stream_wait([w], "weight-gradient all-reduce")
-        return t
+                return t, [w]
+        return t if block or not t.is_cuda else (t, [])
 
     # ---------------------------------------------------------------- step --
     def step(self, compute, pos_own, x_own, W, G_own, stages: Optional[StageEvents] = None):
@@ -323,9 +340,12 @@ class SlabDecomposition:
         mark("halo_header")
         if self.world > 1:
             pl, pr, wp = self.post_ghosts(h, pos_own, "ghost position exchange")
-            self._deadline_wait(wp, "ghost position exchange")
-            self._check_trailers()   # the neighbour list must not see a truncated position message
+            pos_trailers, self._trailers = self._trailers, []
             xl, xr, wx = self.post_ghosts(h, x_own, "ghost feature exchange")  # overlaps the neighbour list
+            self._deadline_wait(wp, "ghost position exchange")
+            feat_trailers, self._trailers = self._trailers, pos_trailers
+            self._check_trailers()   # the neighbour list must not see a truncated position message
+            self._trailers = feat_trailers
             pos_l = torch.cat([pos_own, pl, pr], 0)
         else:
             pos_l = pos_own
@@ -346,9 +366,15 @@ class SlabDecomposition:
         gpos_l = compute.pos_grad(gv, src, dst, graph, pos_l.shape[0])
         mark("pos_grad")
         gW = self.allreduce_sum(gW, block=False)
+        if isinstance(gW, tuple):   # device tensors: the stream waits for it after the reverse halo is posted
+            gW, w_ar = gW
+        else:
+            w_ar = []
         gx_own, gpos_own = self.scatter_ghost_grads(h, [gx_l[:n_own], gpos_l[:n_own]],
-                                                    [gx_l[n_own:], gpos_l[n_own:]])
-        mark("reverse_halo_allreduce")
+                                                    [gx_l[n_own:], gpos_l[n_own:]], mark)
+        if w_ar:
+            self._stream_wait(w_ar, "weight-gradient all-reduce")
+        mark("reverse_sum_allreduce")
         self._finish()
         return out_l[:n_own], gx_own, gW, gpos_own, int(src.numel())
 
