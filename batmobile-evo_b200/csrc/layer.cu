@@ -141,10 +141,18 @@ constexpr int kProdWarps = 4;
 constexpr int kRowBytes = kChunkC * 16 * 4;           // F row of one channel chunk
 constexpr int kSlotBytes = kRowBytes + 160;   // row | Y_e | source index | pad (slot pitch = 8 mod 32 words)
 constexpr int kContrWarps = 4;
-constexpr int kAggProdWarp0 = kLT / 32 + kContrWarps;
+#ifndef BM_AGG_CW
+#define BM_AGG_CW 8
+#endif
+constexpr int kAggCW = BM_AGG_CW;                     // consumer warps
+constexpr int kAggCT = 32 * kAggCW;                   // consumer threads
+constexpr int kCPW = kChunkC / kAggCW;                // channels per consumer warp
+constexpr int kMT = kCPW;                             // its 16-row m-tiles (two channels x 8 m1 each)
+static_assert(kMT % BM_AGG_MQ == 0, "m-tile groups must tile the warp's m-tiles");
+constexpr int kAggProdWarp0 = kAggCW + kContrWarps;
 constexpr int kTiles = BM_AGG_TILES;     // edge-summed tiles handed to the contractors
 constexpr size_t kAggSmem = (size_t)kRing * kSlotBytes + kTiles * kBsBytes + 16;
-constexpr int kAggThreads = kLT + 32 * (kContrWarps + kProdWarps);
+constexpr int kAggThreads = kAggCT + 32 * (kContrWarps + kProdWarps);
 
 // Bounded spin until *turn == want; false (and *err set) after a few seconds.
 __device__ __forceinline__ bool wait_turn(const uint32_t* turn, uint32_t want, int* err) {
@@ -188,10 +196,10 @@ layer_aggregate_kernel(const float* __restrict__ F, int CF, int CPF, const float
     turn = 0;
     for (int i = 0; i < kBufs; ++i) {
       tc::mbar_init(&full[i], 1);
-      tc::mbar_init(&empty[i], kLT / 32);
+      tc::mbar_init(&empty[i], kAggCW);
     }
     for (int i = 0; i < kTiles; ++i) {
-      tc::mbar_init(&bfull[i], kLT / 32);
+      tc::mbar_init(&bfull[i], kAggCW);
       tc::mbar_init(&bempty[i], kContrWarps);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -205,9 +213,9 @@ layer_aggregate_kernel(const float* __restrict__ F, int CF, int CPF, const float
   bool ok = true;
   const int chunks = (CF + kChunkC - 1) / kChunkC;
 
-  if (warp >= kLT / 32 && warp < kAggProdWarp0) {
+  if (warp >= kAggCW && warp < kAggProdWarp0) {
     // ---------------------------------------------------------- contractors
-    const int ct = t - kLT, cp = ct & 31, part = ct >> 5;
+    const int ct = t - kAggCT, cp = ct & 31, part = ct >> 5;
     uint32_t k = 0;
     LD_DECL
     for (int64_t n = blockIdx.x; n < N && ok; n += gridDim.x) {
@@ -325,9 +333,9 @@ layer_aggregate_kernel(const float* __restrict__ F, int CF, int CPF, const float
         // channel's 16 m1 rows), both 8-wide m2 n-tiles; 3xTF32 mma.sync
         const int g = lane >> 2, tq = lane & 3;
         const int cvalid = min(kChunkC, CF - c0);  // channels of this chunk
-        float acc[8][2][4];
+        float acc[kMT][2][4];
 #pragma unroll
-        for (int mt = 0; mt < 8; ++mt)
+        for (int mt = 0; mt < kMT; ++mt)
 #pragma unroll
           for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
@@ -351,11 +359,11 @@ layer_aggregate_kernel(const float* __restrict__ F, int CF, int CPF, const float
           // 2 (mt / 2)), both at m1 = 8 (mt % 2) + row % 8.  All A loads come first
           // (no branches between them and the MMAs); channels past the chunk's
           // last one read as zeros
-          float xr[8][4];
-          const bool fullw = 8 * warp + 8 <= cvalid;
+          float xr[kMT][4];
+          const bool fullw = kCPW * warp + kCPW <= cvalid;
 #pragma unroll
-          for (int mt = 0; mt < 8; ++mt) {
-            const int cc = 8 * warp + 2 * (mt >> 1);
+          for (int mt = 0; mt < kMT; ++mt) {
+            const int cc = kCPW * warp + 2 * (mt >> 1);
             const int o = 16 * cc + 8 * (mt & 1) + g;
             const bool v0 = fullw || cc < cvalid, v1 = fullw || cc + 1 < cvalid;
             xr[mt][0] = v0 ? s0[o] : 0.0f;
@@ -366,7 +374,7 @@ layer_aggregate_kernel(const float* __restrict__ F, int CF, int CPF, const float
           // m-tiles in groups of BM_AGG_MQ, the three terms outermost: 2 BM_AGG_MQ
           // independent accumulators between dependent MMAs (mma.sync latency)
 #pragma unroll
-          for (int mp = 0; mp < 8; mp += BM_AGG_MQ) {
+          for (int mp = 0; mp < kMT; mp += BM_AGG_MQ) {
             uint32_t ah[BM_AGG_MQ][4], al[BM_AGG_MQ][4];
 #pragma unroll
             for (int h = 0; h < BM_AGG_MQ; ++h)
@@ -399,10 +407,10 @@ layer_aggregate_kernel(const float* __restrict__ F, int CF, int CPF, const float
         float* Bs = Bs2 + (size_t)tile * 256 * kTilePitch;
         // tile row (m2 * 16 + m1), column = channel
 #pragma unroll
-        for (int mt = 0; mt < 8; ++mt)
+        for (int mt = 0; mt < kMT; ++mt)
 #pragma unroll
           for (int nt = 0; nt < 2; ++nt) {
-            const int c = 8 * warp + 2 * (mt >> 1), m1 = 8 * (mt & 1) + g, m2 = 8 * nt + 2 * tq;
+            const int c = kCPW * warp + 2 * (mt >> 1), m1 = 8 * (mt & 1) + g, m2 = 8 * nt + 2 * tq;
             *reinterpret_cast<float2*>(Bs + tile_addr(m2 * 16 + m1, c)) = make_float2(acc[mt][nt][0], acc[mt][nt][2]);
             *reinterpret_cast<float2*>(Bs + tile_addr((m2 + 1) * 16 + m1, c)) = make_float2(acc[mt][nt][1], acc[mt][nt][3]);
           }
@@ -736,11 +744,15 @@ constexpr int kTMEpi = kTMCons + kTMProd;                    // first epilogue w
 constexpr int kTMThreads = 32 * (kTMCons + kTMProd + 2);     // two epilogue warps (one per batch parity)
 constexpr int kTMSlot = 4096 + 16;                           // x row slot (bytes): 4 mod 32 words
 constexpr int kTMdBPitch = 1028;                             // dB tile [m2][K] row pitch (floats)
-constexpr int kTMRedPitch = 20;
+#ifndef BM_TM_RED
+#define BM_TM_RED 2
+#endif
+constexpr int kTMRed = BM_TM_RED;                            // partial buffers (batches in the epilogue)
+constexpr int kTMRedPitch = kTMRed == 2 ? 20 : 16;          // 20: conflict-free consumer stores
 constexpr int kTMMeta = 2 * kTBufs;                          // batches of edge metadata in flight                              // partials [warp][edge][m2 (+pad)]
 constexpr size_t kTMRingBytes = (size_t)kTBufs * kBatch * kTMSlot;
 constexpr size_t kTMdBBytes = (size_t)16 * kTMdBPitch * 4;
-constexpr size_t kTMRedBytes = (size_t)2 * kTMCons * kBatch * kTMRedPitch * 4;
+constexpr size_t kTMRedBytes = (size_t)kTMRed * kTMCons * kBatch * kTMRedPitch * 4;
 constexpr size_t kTMSmem = kTMRingBytes + kTdSBytes + kTMdBBytes + kTMRedBytes + 16;
 static_assert(kBatch == 8, "one batch is one 8-wide n-tile of edges");
 
@@ -813,11 +825,11 @@ layer_target_mma_kernel(const float* __restrict__ x, const float* __restrict__ d
   uint8_t* ring = tm_smem;                                                   // [kTBufs * kBatch][kTMSlot]
   float* dSs = reinterpret_cast<float*>(tm_smem + kTMRingBytes);            // [156][64]
   float* dBt = reinterpret_cast<float*>(tm_smem + kTMRingBytes + kTdSBytes);  // [16][kTMdBPitch]
-  float* red = reinterpret_cast<float*>(tm_smem + kTMRingBytes + kTdSBytes + kTMdBBytes);  // [2][16][8][20]
+  float* red = reinterpret_cast<float*>(tm_smem + kTMRingBytes + kTdSBytes + kTMdBBytes);  // [kTMRed][16][8][pitch]
   // edge metadata lives in its own ring of 2 kTBufs batches, released by the
   // epilogue (mempty), so an x-row buffer is free as soon as the consumers are done
   __shared__ TMeta meta[kTMMeta * kBatch];
-  __shared__ uint64_t full[kTBufs], empty[kTBufs], mempty[kTMMeta], dfull, dempty, red_full[2], red_empty[2];
+  __shared__ uint64_t full[kTBufs], empty[kTBufs], mempty[kTMMeta], dfull, dempty, red_full[kTMRed], red_empty[kTMRed];
   __shared__ uint32_t turn;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   if (t == 0) {
@@ -829,7 +841,7 @@ layer_target_mma_kernel(const float* __restrict__ x, const float* __restrict__ d
     for (int i = 0; i < kTMMeta; ++i) tc::mbar_init(&mempty[i], 1);
     tc::mbar_init(&dfull, 1);
     tc::mbar_init(&dempty, kTMCons);  // every consumer warp builds a part of dB
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kTMRed; ++i) {
       tc::mbar_init(&red_full[i], kTMCons);
       tc::mbar_init(&red_empty[i], 1);
     }
@@ -955,12 +967,12 @@ layer_target_mma_kernel(const float* __restrict__ x, const float* __restrict__ d
       const int64_t eb = row_ptr[n], ee = row_ptr[n + 1];
       for (int64_t e0 = eb; e0 < ee && ok; e0 += kBatch, ++bi) {
         const int cnt = (int)imin64(kBatch, ee - e0);
-        const uint32_t par = bi & 1;
+        const uint32_t par = bi & 1, rb = bi % kTMRed;
         if (par != mine) continue;
         LD_MARK()
-        if (!tc::mbar_wait(&red_full[par], (bi >> 1) & 1, err)) { ok = false; break; }
+        if (!tc::mbar_wait(&red_full[rb], (bi / kTMRed) & 1, err)) { ok = false; break; }
         LD_ADD(11)
-        const float* rp = red + (size_t)par * kTMCons * kBatch * kTMRedPitch + je * kTMRedPitch + 4 * mq;
+        const float* rp = red + (size_t)rb * kTMCons * kBatch * kTMRedPitch + je * kTMRedPitch + 4 * mq;
         float4 dq = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int w = 0; w < kTMCons; ++w) {
@@ -969,7 +981,7 @@ layer_target_mma_kernel(const float* __restrict__ x, const float* __restrict__ d
         }
         // the partials are in registers: hand the buffer back before the chain rule
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&red_empty[par]);
+        if (lane == 0) tc::mbar_arrive(&red_empty[rb]);
         float dyv[16];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -1037,13 +1049,13 @@ layer_target_mma_kernel(const float* __restrict__ x, const float* __restrict__ d
       }
       LD_ADD(3)
       for (int64_t e0 = eb; e0 < ee && !stuck; e0 += kBatch, ++bi) {
-        const uint32_t buf = bi % kTBufs, par = bi & 1;
+        const uint32_t buf = bi % kTBufs, rb = bi % kTMRed;
         LD_MARK()
         // warp votes: the warp stays converged and meets the others at the next cons16_sync_or
         if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[buf], (bi / kTBufs) & 1, err))) { stuck = true; break; }
         LD_ADD(4)
-        // red[par] is free once the epilogue has finished the batch two back
-        if (bi >= 2 && !__all_sync(0xffffffffu, tc::mbar_wait(&red_empty[par], ((bi >> 1) - 1) & 1, err))) {
+        // red[rb] is free once the epilogue has finished the batch kTMRed back
+        if (bi >= kTMRed && !__all_sync(0xffffffffu, tc::mbar_wait(&red_empty[rb], ((bi / kTMRed) - 1) & 1, err))) {
           stuck = true;
           break;
         }
@@ -1062,7 +1074,7 @@ layer_target_mma_kernel(const float* __restrict__ x, const float* __restrict__ d
           mma_tf32_16x8x8(acc[s & 1], ah[s], bh0, bh1);
         }
         // partial dY^T: d0 = (m2 g, edge 2t), d1 = (g, 2t+1), d2 = (g+8, 2t), d3 = (g+8, 2t+1)
-        float* rp = red + ((size_t)par * kTMCons + warp) * kBatch * kTMRedPitch;
+        float* rp = red + ((size_t)rb * kTMCons + warp) * kBatch * kTMRedPitch;
         rp[(2 * tq) * kTMRedPitch + g] = acc[0][0] + acc[1][0];
         rp[(2 * tq + 1) * kTMRedPitch + g] = acc[0][1] + acc[1][1];
         rp[(2 * tq) * kTMRedPitch + g + 8] = acc[0][2] + acc[1][2];
@@ -1071,7 +1083,7 @@ layer_target_mma_kernel(const float* __restrict__ x, const float* __restrict__ d
         LD_ADD(6)
         if (lane == 0) {
           tc::mbar_arrive(&empty[buf]);
-          tc::mbar_arrive(&red_full[par]);
+          tc::mbar_arrive(&red_full[rb]);
         }
       }
     }
