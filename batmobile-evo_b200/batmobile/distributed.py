@@ -123,7 +123,10 @@ class SlabDecomposition:
         near_right = self.hi - c < self.reach
         if self.world == 2:
             near_right = near_right & ~near_left
-        return torch.nonzero(near_left).flatten(), torch.nonzero(near_right).flatten()
+        both = torch.stack([near_left, near_right], 0)
+        nl, nr = (int(v) for v in both.sum(1).cpu().tolist())   # the one host read of the face lists
+        idx = torch.nonzero_static(both, size=nl + nr)[:, 1]      # row-major: the left list, then the right
+        return idx[:nl], idx[nl:]
 
     # ------------------------------------------------------ waits, failure --
     def abort(self):
@@ -147,11 +150,14 @@ class SlabDecomposition:
         end = None if self.timeout is None else time.monotonic() + self.timeout
         try:
             if end is not None and dist.get_backend(self.group) == "nccl":
+                spin_end = time.monotonic() + 2e-3   # poll without sleeping first (a sleep costs ~0.1 ms)
                 while not all(w.is_completed() for w in works):
-                    if time.monotonic() > end:
+                    now = time.monotonic()
+                    if now > end:
                         raise self._fail(what, "did not complete within %.1f s: a peer left, never sent, or sent "
                                                "a message of another size" % self.timeout)
-                    time.sleep(2e-5)
+                    if now > spin_end:
+                        time.sleep(1e-4)
             for w in works:
                 if end is None:
                     w.wait()
